@@ -1,0 +1,442 @@
+"""Benchmark of the B200 paged-decode path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2|cfg1|cfg4] [--split TOKENS]
+
+A step is one batched decode (qvp_decode: the decode kernel plus, when a
+context is split, the combine kernel) over the workload's whole batch, with
+the block pool, tables and queries resident in HBM. The default workload is
+the Qwen2-VL-7B-shaped config (cfg2: 64 sequences, ctx ~ U[512, 8192], 28/4
+heads, head_dim 128, bf16), whose K/V (~570 MB) exceeds the 126 MB L2, so no
+flush is needed between steps.
+
+Metric: algorithmic bytes per step (K + V of every context token, Q, out and
+the table entries used) / step time, in GB/s, plus sequences/s.
+
+Multi-GPU (torchrun, one rank per GPU): cfg2 runs one independent batch per
+rank (different seeds, no collective on the data path, weak scaling); cfg4
+shards the kv heads of one batch across ranks (strong scaling).
+
+`--impl reference` times the reference's own CPU paged_attention_decode<T>
+(oracle/_ref, compiled from the reference sources; the C restatement when
+that library is absent) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "qwenvl-paged_b200"), os.path.join(ROOT, "oracle")]
+
+import numpy as np  # noqa: E402
+
+import workloads as W  # noqa: E402
+
+METRIC = "paged-decode KV GB/s (% of HBM peak) and seqs/s at 1/2/4/8 B200 vs host CPU"
+FALLBACK_HBM_GBS = 6650.0
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode step of the
+# default workload, from the ncu capture summarised in
+# profiles/paged_decode_fast_cfg2.md (None until captured).
+NCU_TRAFFIC_BYTES = {}
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def dist_env():
+    return int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")), int(
+        os.environ.get("LOCAL_RANK", "0"))
+
+
+def make_workload(name, rank, world, gpus):
+    if name == "cfg2":
+        return W.cfg2(seed=2 + rank), "weak"
+    if name == "cfg1":
+        return W.cfg1(seed=1 + rank), "weak"
+    if name == "cfg4":
+        shards = max(world, 1)
+        return W.cfg4(shards=shards), "strong"
+    raise SystemExit(f"unknown workload {name}")
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling while a region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.lines += [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for l in self.lines:
+            parts = [p.strip() for p in l.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def run_ours(args):
+    import torch
+
+    import qvp
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    w, scaling = make_workload(args.workload, rank, world, args.gpus)
+    torch_dtype = torch.bfloat16 if w.dtype == "bf16" else torch.float32
+
+    # inputs generated on the device from a seed, resident in HBM
+    g = torch.Generator(device=dev)
+    g.manual_seed(w.seed * 1000 + 7)
+    pool = torch.zeros(w.num_blocks * w.block_stride // w.elem, dtype=torch_dtype, device=dev)
+    pool.view(w.num_blocks, -1)[:, : w.block_bytes // w.elem].normal_(generator=g)
+    q = torch.randn(w.batch, w.num_query_heads, w.head_dim, generator=g, device=dev, dtype=torch.float32).to(
+        torch_dtype)
+    out = torch.empty_like(q)
+    ctx_d = torch.from_numpy(w.context_lens).to(dev)
+    tab_d = torch.from_numpy(w.tables).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    shape = qvp.make_shape(w.tokens_per_block, w.num_layers, w.num_kv_heads, w.head_dim, w.elem)
+    a = qvp.decode_args(pool=pool.data_ptr(), block_stride=w.block_stride, num_blocks=w.num_blocks, shape=shape,
+                        dtype=qvp.DTYPE_BF16 if w.dtype == "bf16" else qvp.DTYPE_F32, layer=0,
+                        num_query_heads=w.num_query_heads, scale=w.scale, batch=w.batch,
+                        max_blocks_per_seq=w.pitch, max_context_len=w.max_context_len,
+                        block_tables=tab_d.data_ptr(), context_lens=ctx_d.data_ptr(), query=q.data_ptr(),
+                        out=out.data_ptr(), split_tokens=args.split, error_word=err.data_ptr())
+    plan = qvp.decode_plan(a)
+    ws = None
+    if plan["workspace_bytes"]:
+        ws = torch.empty(plan["workspace_bytes"], dtype=torch.uint8, device=dev)
+        a.workspace = ws.data_ptr()
+        a.workspace_bytes = plan["workspace_bytes"]
+    stream = torch.cuda.current_stream()
+    sh = stream.cuda_stream
+    launches_per_step = 1 + (1 if plan["num_splits"] > 1 else 0)
+
+    def step():
+        st = qvp.decode(a, sh)
+        if st != 0:
+            raise RuntimeError(f"qvp_decode failed: {st} {qvp.last_error()}")
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def timed(fn, steps):
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        ms = e0.elapsed_time(e1)
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    total_ms = timed(step, args.steps)
+    # Clocks: the timed region of a short run can be shorter than the sampling
+    # period, so keep the same step running untimed until ~1 s has elapsed.
+    t_end = time.time() + 1.0
+    while time.time() < t_end:
+        for _ in range(50):
+            step()
+        torch.cuda.synchronize()
+    sampler.stop()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"decode kernel reported device error bits {int(err.item())}")
+
+    ms_step = total_ms / args.steps
+    alg = w.algorithmic_bytes()
+    world_bytes = alg * (world if scaling == "weak" else 1)
+    value = world_bytes / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    achieved = alg / (ms_step * 1e-3) / 1e9  # per GPU
+
+    # e2e through the C ABI with host buffers: per step, H2D of this step's
+    # queries, block tables and context lengths from pinned memory, the decode,
+    # and the D2H of the outputs, all inside the timed region.
+    q_h = q.cpu().pin_memory()
+    tab_h = torch.from_numpy(w.tables).pin_memory()
+    ctx_h = torch.from_numpy(w.context_lens).pin_memory()
+    out_h = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        q.copy_(q_h, non_blocking=True)
+        tab_d.copy_(tab_h, non_blocking=True)
+        ctx_d.copy_(ctx_h, non_blocking=True)
+        step()
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_ms = timed(e2e_step, args.steps) / args.steps
+    h2d = q.numel() * q.element_size() + w.tables.nbytes + w.context_lens.nbytes
+    d2h = out.numel() * out.element_size()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        host_pool = pool.view(torch.uint8).cpu().numpy() if w.elem == 2 else pool.cpu().numpy().view(np.uint8)
+        host_q = q.cpu().view(torch.int16).numpy().view(np.uint16) if w.dtype == "bf16" else q.cpu().numpy()
+        cpu = cpu_baseline(w, host_pool.reshape(-1), host_q, budget_s=args.cpu_budget)
+
+    if rank == 0:
+        traffic = NCU_TRAFFIC_BYTES.get(w.name)
+        line = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True,
+            "scaling": scaling,
+            "vs_baseline": None,
+            "dtype": w.dtype,
+            "data": "synthetic: seeded N(0,1) K/V/Q, seeded context lengths and scattered block tables",
+            "config": {
+                "workload": w.name,
+                "batch_per_gpu": w.batch,
+                "global_batch": w.batch * (world if scaling == "weak" else 1),
+                "context_lens": f"{int(w.context_lens.min())}..{int(w.context_lens.max())} "
+                                f"(sum {int(w.context_lens.sum())})",
+                "heads": f"{w.num_query_heads}q/{w.num_kv_heads}kv per GPU",
+                "head_dim": w.head_dim,
+                "tokens_per_block": w.tokens_per_block,
+                "pool_blocks": w.num_blocks,
+                "split_tokens": plan["split_tokens"],
+                "num_splits_max": plan["num_splits"],
+                "kernel": "paged_decode_fast (TMA + mma.sync)" if plan["fast"] else "paged_decode_generic",
+                "l2": f"inputs larger than L2 ({w.kv_bytes() / 1e6:.0f} MB of K/V read per step)",
+                "parallelism": f"dp{world}" if scaling == "weak" else f"kv-head shards x{world}",
+            },
+            "seqs_per_s": round(w.batch * (world if scaling == "weak" else 1) / (ms_step * 1e-3), 1),
+            "roofline": {
+                "bound": "hbm",
+                "achieved": round(achieved, 1),
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4),
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                else "fallback 6.65 TB/s",
+                "traffic": traffic,
+                "kernel": "decode step = paged_decode_fast + combine_partitions, CUDA events, mean over steps",
+                "algorithmic_bytes_per_step": alg,
+            },
+            "e2e": {
+                "value": round(world_bytes / (e2e_ms * 1e-3) / 1e9, 2),
+                "unit": "GB/s",
+                "ms_per_step": round(e2e_ms, 5),
+                "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h),
+                "path": "C ABI qvp_decode with pinned-host q/tables/ctx in, out back, per step",
+            },
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": sampler.summary(),
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(w, pool, q, budget_s=15.0, threads=None):
+    """Times the reference CPU path (or the C restatement) on a bounded
+    sample of the same workload: the first sequences of the batch, repeated
+    until about `budget_s` seconds of wall time."""
+    import oracle
+
+    threads = threads or cpu_threads()
+    kind = "reference" if oracle.ref_available() else "port"
+    n = w.batch
+    sub = W.DecodeWorkload(w.name, w.tokens_per_block, w.num_layers, w.num_kv_heads, w.head_dim, w.dtype,
+                           w.num_query_heads, w.scale, w.context_lens[:n].copy(), w.tables[:n].copy(),
+                           w.num_blocks, w.seed)
+    if kind == "reference":
+        r = oracle.RefDecoder(sub, pool)
+        r.bind()
+        run = lambda: r.decode(q[:n], threads=threads)  # noqa: E731
+    else:
+        run = lambda: oracle.port_decode(sub, pool, q[:n], threads=threads)  # noqa: E731
+    t0 = time.perf_counter()
+    _, status = run()
+    first = time.perf_counter() - t0
+    reps = max(1, min(50, int(budget_s / max(first, 1e-6))))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        run()
+    dt = (time.perf_counter() - t0) / reps
+    if kind == "reference":
+        r.close()
+    return {"value": round(sub.algorithmic_bytes() / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
+            "kind": kind, "ms_per_step": round(dt * 1e3, 3), "seqs_per_s": round(n / dt, 2),
+            "sample": f"all {n} sequences of {w.name} (same seeded bytes as the GPU run), "
+                      f"{reps} repetitions after 1 untimed, {threads} threads, "
+                      f"all_ok={bool(status.all())}"}
+
+
+def run_reference(args):
+    """The reference CPU decode on the host cores (rank 0 only)."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle
+
+    w, scaling = make_workload(args.workload, 0, 1, 1)
+    pool, q = W.host_inputs(w)
+    threads = cpu_threads()
+    kind = "reference" if oracle.ref_available() else "port"
+    if kind == "reference":
+        r = oracle.RefDecoder(w, pool)
+        r.bind()
+        fn = lambda: r.decode(q, threads=threads)  # noqa: E731
+    else:
+        fn = lambda: oracle.port_decode(w, pool, q, threads=threads)  # noqa: E731
+    # size the sample so the whole run stays within a few minutes
+    t0 = time.perf_counter()
+    _, status = fn()
+    one = time.perf_counter() - t0
+    n_seq = w.batch
+    if one * (args.steps + args.warmup) > 150.0:
+        n_seq = max(1, int(w.batch * 150.0 / (one * (args.steps + args.warmup))))
+    sub = W.DecodeWorkload(w.name, w.tokens_per_block, w.num_layers, w.num_kv_heads, w.head_dim, w.dtype,
+                           w.num_query_heads, w.scale, w.context_lens[:n_seq].copy(), w.tables[:n_seq].copy(),
+                           w.num_blocks, w.seed)
+    if kind == "reference":
+        r.bind(sub.context_lens, sub.tables)
+        fn = lambda: r.decode(q[:n_seq], threads=threads)  # noqa: E731
+    else:
+        fn = lambda: oracle.port_decode(sub, pool, q[:n_seq], threads=threads)  # noqa: E731
+    for _ in range(args.warmup):
+        fn()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        fn()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = sub.algorithmic_bytes() / dt / 1e9
+    sample = f"{n_seq} of {w.batch} sequences of {w.name} per step, {threads} threads"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(value, 4),
+        "unit": "GB/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 3),
+        "higher_is_better": True,
+        "scaling": scaling,
+        "vs_baseline": None,
+        "dtype": w.dtype,
+        "data": "synthetic: seeded N(0,1) K/V/Q, seeded context lengths and scattered block tables",
+        "config": {"workload": w.name, "batch": n_seq, "heads": f"{w.num_query_heads}q/{w.num_kv_heads}kv",
+                   "head_dim": w.head_dim, "tokens_per_block": w.tokens_per_block},
+        "seqs_per_s": round(n_seq / dt, 2),
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    if kind == "reference":
+        r.close()
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=10)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--workload", choices=["cfg2", "cfg1", "cfg4"], default="cfg2")
+    p.add_argument("--split", type=int, default=0, help="split-K partition in tokens (0 = auto)")
+    p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = p.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

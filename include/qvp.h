@@ -1,0 +1,208 @@
+/*
+ * qvp.h - C ABI of the B200 paged-decode path (sm_100a).
+ *
+ * Every entry point takes plain pointers and sizes, never a C++ or torch type,
+ * so any FFI (ctypes, cgo, JNI, N-API) can bind it. All device work is enqueued
+ * on the caller's stream; no call synchronises the device unless its comment
+ * says so. Nothing here is thread-safe: like the C++ API it serves, it is meant
+ * to be driven from one engine thread.
+ *
+ * Status convention: every function returns a qvp_status (0 = success). On a
+ * non-zero status that was detected on the host, no device work was enqueued
+ * and no output buffer was touched.
+ *
+ * Reference interfaces each group replaces (paths inside the reference project
+ * phhuang191129/QwenVL-Paged):
+ *   - decode:      include/qwenvl_paged/PagedAttention.h:53-127
+ *                  (paged_attention_decode<T>) and PagedAttention.h:23-28
+ *                  (PagedAttentionParams)
+ *   - layout:      include/qwenvl_paged/CacheLayout.h:40-79, src/CacheLayout.cpp:5-38
+ *   - block bytes: src/Block.cpp:8-13 (BlockShape::byte_size), Block.cpp:30-44
+ *                  (size rounded up to the 256-byte alignment)
+ *   - block copy:  src/MemoryAllocator.cpp:76-85 (copy_block)
+ *   - swap bytes:  src/SwapBackend.cpp:10-39 (HostSwapBackend::store / load)
+ */
+#ifndef QVP_H
+#define QVP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QVP_API __attribute__((visibility("default")))
+#else
+#define QVP_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t / CUstream; NULL is the legacy default stream. */
+typedef struct CUstream_st* qvp_stream_t;
+
+typedef enum qvp_status {
+    QVP_OK = 0,
+    QVP_ERR_INVALID = 1,      /* arguments inconsistent with the cache shape     */
+    QVP_ERR_UNMAPPED = 2,     /* a block in [0, context) is unmapped or swapped  */
+    QVP_ERR_CUDA = 3,         /* a CUDA runtime call failed (see qvp_last_error) */
+    QVP_ERR_DEVICE = 4,       /* a kernel reported a bad block id or a timeout   */
+    QVP_ERR_NOMEM = 5,        /* device or pinned allocation failed              */
+    QVP_ERR_UNSUPPORTED = 6,  /* shape outside what the kernels implement        */
+    QVP_ERR_WORKSPACE = 7     /* caller workspace smaller than required          */
+} qvp_status;
+
+typedef enum qvp_dtype {
+    QVP_DTYPE_F32 = 0,   /* 4-byte IEEE float            */
+    QVP_DTYPE_BF16 = 1   /* 2-byte bfloat16, fp32 math   */
+} qvp_dtype;
+
+/*
+ * Shape of one physical block. Field for field the reference BlockShape
+ * (include/qwenvl_paged/Block.h:46-57). Elements inside a block are ordered
+ * [layer][K|V][token_in_block][kv_head][head_dim] (src/CacheLayout.cpp:5-19).
+ */
+typedef struct qvp_block_shape {
+    uint32_t tokens_per_block;
+    uint32_t num_layers;
+    uint32_t num_kv_heads;
+    uint32_t head_dim;
+    uint32_t bytes_per_element;
+} qvp_block_shape;
+
+/* BlockShape::byte_size(): tokens * layers * kv_heads * head_dim * elem * 2. */
+QVP_API size_t qvp_block_bytes(const qvp_block_shape* shape);
+/* Distance between two physical blocks in a pool: byte_size rounded up to 256
+ * (the reference rounds each block allocation the same way, Block.cpp:30-44). */
+QVP_API size_t qvp_block_stride(const qvp_block_shape* shape);
+
+/* Human-readable text of the last error raised on this thread. */
+QVP_API const char* qvp_last_error(void);
+/* Library version string, e.g. "qvp 0.1.0 sm_100a". */
+QVP_API const char* qvp_version(void);
+/* Number of SMs of the current device, 0 when no device is visible. */
+QVP_API int qvp_device_sm_count(void);
+
+/* ---------------------------------------------------------------------------
+ * Block pool: one cudaMalloc'd slab per GPU. Block i lives at base + i*stride.
+ * Replaces the per-block aligned_alloc of PhysicalBlock (src/Block.cpp:30-44);
+ * the whole pool is zero-filled once at creation.
+ * ------------------------------------------------------------------------- */
+typedef struct qvp_pool qvp_pool;
+
+QVP_API int qvp_pool_create(int device, const qvp_block_shape* shape, uint32_t num_blocks,
+                    qvp_pool** out_pool);
+QVP_API int qvp_pool_destroy(qvp_pool* pool);
+QVP_API void* qvp_pool_base(const qvp_pool* pool);
+QVP_API size_t qvp_pool_stride(const qvp_pool* pool);
+QVP_API uint32_t qvp_pool_num_blocks(const qvp_pool* pool);
+QVP_API int qvp_pool_device(const qvp_pool* pool);
+/* Synchronous helpers for tests and set-up: copy `bytes` between host memory
+ * and block `block` at byte `offset`. Bounds are checked against the stride. */
+QVP_API int qvp_pool_write(qvp_pool* pool, uint32_t block, size_t offset, const void* host,
+                   size_t bytes);
+QVP_API int qvp_pool_read(const qvp_pool* pool, uint32_t block, size_t offset, void* host,
+                  size_t bytes);
+
+/* ---------------------------------------------------------------------------
+ * Batched paged decode.
+ *
+ * For every sequence b in [0, batch) and query head h in [0, num_query_heads):
+ *   kv = h / (num_query_heads / num_kv_heads)
+ *   s_t = scale * <q[b,h,:], K[b, layer, t, kv, :]>      for t < context_lens[b]
+ *   out[b,h,:] = sum_t softmax(s)_t * V[b, layer, t, kv, :]
+ * which is paged_attention_decode<T> (PagedAttention.h:94-124) applied to every
+ * sequence of the batch at once. Token t of sequence b lives in physical block
+ * block_tables[b * max_blocks_per_seq + t / tokens_per_block], slot
+ * t % tokens_per_block.
+ *
+ * Checks done on the host (status returned, nothing enqueued): shape, dtype,
+ * layer < num_layers, num_query_heads a positive multiple of num_kv_heads,
+ * context lengths bounded by max_context_len <= max_blocks_per_seq*tokens.
+ * The device tables are not read on the host: a table entry outside
+ * [0, num_blocks) inside a context makes the kernel record a non-zero value in
+ * *error_word (when given) and read block 0 instead, so no access leaves the
+ * pool; the output of that sequence is then unspecified. Callers that need the
+ * reference's "refuse and leave out untouched" behaviour validate the tables
+ * on the host first (the C++ layer does).
+ *
+ * Split-K: contexts longer than split_tokens are cut into partitions whose
+ * partial (max, sum, accumulator) go to `workspace` and are merged by a second
+ * kernel. split_tokens = 0 picks a size from the batch shape.
+ * ------------------------------------------------------------------------- */
+typedef struct qvp_decode_args {
+    const void* pool;              /* device base of the block pool            */
+    size_t block_stride;           /* bytes between physical blocks            */
+    uint32_t num_blocks;           /* pool capacity in blocks                  */
+    qvp_block_shape shape;         /* shape shared by every block              */
+    int32_t dtype;                 /* qvp_dtype of K/V, query and out          */
+    uint32_t layer;                /* PagedAttentionParams::layer              */
+    uint32_t num_query_heads;      /* PagedAttentionParams::num_query_heads    */
+    float scale;                   /* PagedAttentionParams::scale              */
+    uint32_t batch;                /* number of sequences                      */
+    uint32_t max_blocks_per_seq;   /* row pitch of block_tables                */
+    uint32_t max_context_len;      /* host-known upper bound of context_lens   */
+    const int32_t* block_tables;   /* device int32 [batch][max_blocks_per_seq] */
+    const int32_t* context_lens;   /* device int32 [batch], each in [1, max]   */
+    const void* query;             /* device [batch][num_query_heads][head_dim]*/
+    void* out;                     /* device [batch][num_query_heads][head_dim]*/
+    uint32_t split_tokens;         /* 0 = auto; fast path: a multiple of 16    */
+    void* workspace;               /* device scratch, >= qvp_decode_workspace_size */
+    size_t workspace_bytes;
+    int32_t* error_word;           /* device int32 or NULL; never cleared here */
+} qvp_decode_args;
+
+/* Scratch bytes `qvp_decode` needs for these arguments (0 when no split). */
+QVP_API int qvp_decode_workspace_size(const qvp_decode_args* args, size_t* bytes);
+/* The split size `qvp_decode` would use for these arguments. */
+QVP_API int qvp_decode_plan(const qvp_decode_args* args, uint32_t* split_tokens,
+                    uint32_t* num_splits, int* fast_path);
+QVP_API int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Block movers.
+ *
+ * qvp_copy_blocks: for i < n, copy `bytes` from block pairs[2i] to block
+ * pairs[2i+1] of the same pool (MemoryAllocator::copy_block, called by
+ * copy-on-write at src/KVCacheManager.cpp:146). `pairs` is device int32.
+ * One launch for the whole batch.
+ *
+ * qvp_gather_blocks / qvp_scatter_blocks: move the blocks named by the device
+ * int32 list `ids` between the pool and a contiguous buffer `staging`
+ * (staging + i*bytes). `staging` may be device memory or pinned host memory
+ * mapped into the device's address space. These carry the bytes of
+ * HostSwapBackend::store / load (src/SwapBackend.cpp:10-39).
+ *
+ * Ids outside [0, num_blocks) are skipped and recorded in *error_word.
+ * ------------------------------------------------------------------------- */
+QVP_API int qvp_copy_blocks(void* pool, size_t block_stride, uint32_t num_blocks, size_t bytes,
+                    const int32_t* pairs, uint32_t n, int32_t* error_word,
+                    qvp_stream_t stream);
+QVP_API int qvp_gather_blocks(const void* pool, size_t block_stride, uint32_t num_blocks,
+                      size_t bytes, const int32_t* ids, uint32_t n, void* staging,
+                      int32_t* error_word, qvp_stream_t stream);
+QVP_API int qvp_scatter_blocks(void* pool, size_t block_stride, uint32_t num_blocks,
+                       size_t bytes, const int32_t* ids, uint32_t n,
+                       const void* staging, int32_t* error_word, qvp_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * KV append: write one new token's K and V for every kv head of every
+ * sequence: for b < batch, token position positions[b] of sequence b goes to
+ * block block_tables[b*pitch + pos/tokens_per_block], slot pos%tokens_per_block,
+ * layer `layer`. k and v are device [batch][num_kv_heads][head_dim] in the
+ * pool's element type. This is the device form of the per-token writes that
+ * the reference performs through ensure_token_writable and a host store
+ * (tests/PagedAttention.test.cpp:97-127); call it only after copy-on-write has
+ * made every target block private.
+ * ------------------------------------------------------------------------- */
+QVP_API int qvp_kv_append(void* pool, size_t block_stride, uint32_t num_blocks,
+                  const qvp_block_shape* shape, uint32_t layer, uint32_t batch,
+                  uint32_t max_blocks_per_seq, const int32_t* block_tables,
+                  const int32_t* positions, const void* k, const void* v,
+                  int32_t* error_word, qvp_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QVP_H */

@@ -1,0 +1,158 @@
+"""TEST INFRASTRUCTURE ONLY - Python handles on the CPU oracle.
+
+Loaded only by tests/, __graft_entry__.smoke() and bench.py (as the checker
+and as the timed CPU baseline). Two back ends:
+
+  * ``port``      - oracle/lib/liboracle.so, the plain-C restatement of
+                    paged_attention_decode<T> (paged_decode_oracle.c).
+  * ``reference`` - oracle/_ref/libqvp_ref.so, the reference's own sources
+                    (phhuang191129/QwenVL-Paged src/*.cpp and
+                    include/qwenvl_paged/PagedAttention.h) compiled by
+                    oracle/Makefile. Present wherever it was built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_PATH = os.path.join(_HERE, "lib", "liboracle.so")
+REF_PATH = os.path.join(_HERE, "_ref", "libqvp_ref.so")
+
+
+class Shape(C.Structure):
+    _fields_ = [("tokens_per_block", C.c_uint32), ("num_layers", C.c_uint32), ("num_kv_heads", C.c_uint32),
+                ("head_dim", C.c_uint32), ("bytes_per_element", C.c_uint32)]
+
+
+_port = None
+_ref = None
+
+
+def port_lib() -> C.CDLL:
+    global _port
+    if _port is None:
+        if not os.path.exists(PORT_PATH):
+            raise ImportError(f"{PORT_PATH} missing; run `make -C oracle`")
+        lib = C.CDLL(PORT_PATH)
+        vp, u32 = C.c_void_p, C.c_uint32
+        lib.oracle_paged_decode.restype = C.c_int
+        lib.oracle_paged_decode.argtypes = [vp, C.c_size_t, u32, C.POINTER(Shape), C.c_int, u32, u32, C.c_float,
+                                            vp, u32, u32, vp, vp]
+        lib.oracle_paged_decode_batch.restype = C.c_int
+        lib.oracle_paged_decode_batch.argtypes = [vp, C.c_size_t, u32, C.POINTER(Shape), C.c_int, u32, u32,
+                                                  C.c_float, u32, u32, vp, vp, vp, vp, vp, C.c_int]
+        lib.oracle_copy_blocks.restype = None
+        lib.oracle_copy_blocks.argtypes = [vp, C.c_size_t, u32, C.c_size_t, vp, u32]
+        _port = lib
+    return _port
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH)
+
+
+def ref_lib() -> C.CDLL:
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_PATH):
+            raise ImportError(f"{REF_PATH} missing; build it with `make -C oracle` where the reference exists")
+        lib = C.CDLL(REF_PATH)
+        vp, u32 = C.c_void_p, C.c_uint32
+        lib.ref_pool_create.restype = vp
+        lib.ref_pool_create.argtypes = [C.POINTER(Shape), u32, vp, C.c_size_t]
+        lib.ref_pool_destroy.restype = None
+        lib.ref_pool_destroy.argtypes = [vp]
+        lib.ref_tables_create.restype = vp
+        lib.ref_tables_create.argtypes = [vp, u32, u32, vp, vp]
+        lib.ref_tables_destroy.restype = None
+        lib.ref_tables_destroy.argtypes = [vp]
+        lib.ref_decode_bound.restype = C.c_int
+        lib.ref_decode_bound.argtypes = [vp, vp, C.c_int, u32, u32, C.c_float, u32, vp, vp, vp, vp, C.c_int]
+        lib.ref_decode_batch.restype = C.c_int
+        lib.ref_decode_batch.argtypes = [vp, C.c_int, u32, u32, C.c_float, u32, u32, vp, vp, vp, vp, vp, C.c_int]
+        if hasattr(lib, "ref_replay"):
+            lib.ref_replay.restype = C.c_int
+            lib.ref_replay.argtypes = [C.c_char_p, C.c_char_p, C.c_size_t]
+        _ref = lib
+    return _ref
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def _shape(w) -> Shape:
+    return Shape(w.tokens_per_block, w.num_layers, w.num_kv_heads, w.head_dim, w.elem)
+
+
+def port_decode(w, pool: np.ndarray, q: np.ndarray, threads: int = 1, context_lens=None, tables=None):
+    """Oracle outputs (float32 [B, Hq, D]) and per-sequence status."""
+    ctx = np.ascontiguousarray(w.context_lens if context_lens is None else context_lens, dtype=np.int32)
+    tab = np.ascontiguousarray(w.tables if tables is None else tables, dtype=np.int32)
+    pool = np.ascontiguousarray(pool)
+    q = np.ascontiguousarray(q)
+    out = np.zeros((len(ctx), w.num_query_heads, w.head_dim), dtype=np.float32)
+    status = np.zeros(len(ctx), dtype=np.int32)
+    sh = _shape(w)
+    port_lib().oracle_paged_decode_batch(_ptr(pool), w.block_stride, w.num_blocks, C.byref(sh),
+                                         0 if w.dtype == "f32" else 1, w.layer, w.num_query_heads, w.scale,
+                                         len(ctx), tab.shape[1], _ptr(tab), _ptr(ctx), _ptr(q), _ptr(out),
+                                         _ptr(status), threads)
+    return out, status
+
+
+class RefDecoder:
+    """The reference's paged_attention_decode<T> over a copy of the pool."""
+
+    def __init__(self, w, pool: np.ndarray):
+        self.w = w
+        self.lib = ref_lib()
+        self.sh = _shape(w)
+        pool = np.ascontiguousarray(pool)
+        self.h = self.lib.ref_pool_create(C.byref(self.sh), w.num_blocks, _ptr(pool), w.block_stride)
+        self.tables_h = None
+
+    def bind(self, context_lens=None, tables=None):
+        w = self.w
+        self.ctx = np.ascontiguousarray(w.context_lens if context_lens is None else context_lens, dtype=np.int32)
+        self.tab = np.ascontiguousarray(w.tables if tables is None else tables, dtype=np.int32)
+        if self.tables_h is not None:
+            self.lib.ref_tables_destroy(self.tables_h)
+        self.tables_h = self.lib.ref_tables_create(self.h, len(self.ctx), self.tab.shape[1], _ptr(self.tab),
+                                                   _ptr(self.ctx))
+
+    def decode(self, q: np.ndarray, threads: int = 1):
+        """Outputs in the workload dtype (bf16 as uint16 bits) and status."""
+        w = self.w
+        if self.tables_h is None:
+            self.bind()
+        q = np.ascontiguousarray(q)
+        out = np.zeros((len(self.ctx), w.num_query_heads, w.head_dim),
+                       dtype=np.float32 if w.dtype == "f32" else np.uint16)
+        status = np.zeros(len(self.ctx), dtype=np.int32)
+        self.lib.ref_decode_bound(self.h, self.tables_h, 0 if w.dtype == "f32" else 1, w.layer,
+                                  w.num_query_heads, w.scale, len(self.ctx), _ptr(self.ctx), _ptr(q), _ptr(out),
+                                  _ptr(status), threads)
+        return out, status
+
+    def close(self):
+        if self.tables_h is not None:
+            self.lib.ref_tables_destroy(self.tables_h)
+            self.tables_h = None
+        if self.h:
+            self.lib.ref_pool_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def port_copy_blocks(pool: np.ndarray, block_stride: int, num_blocks: int, nbytes: int, pairs: np.ndarray):
+    pairs = np.ascontiguousarray(pairs, dtype=np.int32)
+    port_lib().oracle_copy_blocks(_ptr(pool), block_stride, num_blocks, nbytes, _ptr(pairs), len(pairs) // 2)

@@ -1,0 +1,791 @@
+// Batched paged-decode attention for B200 (sm_100a).
+//
+// Computes, for every sequence of a batch and every query head, what the
+// reference CPU kernel paged_attention_decode<T> computes for one sequence
+// (phhuang191129/QwenVL-Paged include/qwenvl_paged/PagedAttention.h:53-127):
+//   kv = h / G;  s_t = scale * <q_h, K_t>;  out_h = sum_t softmax(s)_t V_t
+// with fp32 accumulation. The reference takes an exact max and then sums
+// exp(s - max) (PagedAttention.h:98-118); here each partition keeps a running
+// (max, sum, accumulator) and rescales when the max grows, which is the same
+// value in exact arithmetic. Partitions of long contexts (split-K) are merged
+// by `combine_partitions`.
+//
+// Two kernels:
+//  * paged_decode_fast: bf16 K/V/Q, 16-token blocks, head_dim 64 or 128,
+//    at most 16 query heads per kv head, unpadded blocks. One CTA owns
+//    (sequence, partition, group of HH kv heads). A producer warp streams each
+//    block's K and V slices for the CTA's heads into shared memory with TMA
+//    tensor copies (128-byte swizzle, mbarrier completion, evict-first L2
+//    hint); eight consumer warps each own one kv head and every J-th block and
+//    run QK^T and PV as m16n8k16 bf16 tensor-core products with the GQA group
+//    padded to 16 rows, so one K/V load serves the whole query group.
+//  * paged_decode_generic: any element type, block size, head_dim <= 256 and
+//    group size; one CTA per (sequence, partition, query head), four warps
+//    striding over tokens, lanes over head_dim, exact expf.
+#include "qvp_device.cuh"
+#include "qvp_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstring>
+
+namespace qvp {
+
+namespace {
+
+constexpr int kFastComputeWarps = 8;
+constexpr int kFastThreads = (kFastComputeWarps + 1) * 32;
+constexpr int kGenericWarps = 4;
+constexpr int kGenericMaxDimPerLane = 8;  // head_dim <= 256
+
+struct FastParams {
+    const int32_t* tables;
+    const int32_t* ctx;
+    const __nv_bfloat16* q;
+    __nv_bfloat16* out;
+    float* ws_o;
+    float2* ws_ml;
+    int32_t* err;
+    uint32_t pitch;
+    uint32_t num_blocks;
+    uint32_t layer;
+    uint32_t num_layers;
+    uint32_t hq;
+    uint32_t group;
+    uint32_t split_blocks;
+    uint32_t max_splits;
+    float scale_log2;
+};
+
+template <int D, int HH, int STAGES>
+struct FastShape {
+    static constexpr int J = kFastComputeWarps / HH;     // blocks in flight per stage
+    static constexpr uint32_t kBox = HH * 16 * D * 2;   // one stream of one block, HH heads
+    static constexpr uint32_t kBlock = 2 * kBox;        // K and V
+    static constexpr uint32_t kStage = J * kBlock;
+    static constexpr uint32_t kSmem = STAGES * kStage + 1024 + 2 * STAGES * 8 + 16;
+};
+
+// Byte address of element chunk `chunk` (8 bf16) of token `t` inside the
+// swizzled box [dh][hh][t][64] written by TMA with 128-byte swizzle.
+__device__ __forceinline__ uint32_t box_addr(uint32_t base, int row_group, int t, int chunk) {
+    const int r = row_group * 16 + t;
+    return base + static_cast<uint32_t>(r * 128 + ((chunk ^ (t & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t mask_pair(uint32_t x, int t0, int valid) {
+    const uint32_t lo = (t0 < valid) ? 0x0000FFFFu : 0u;
+    const uint32_t hi = (t0 + 1 < valid) ? 0xFFFF0000u : 0u;
+    return x & (lo | hi);
+}
+
+template <int D, int HH, int STAGES>
+__global__ void __launch_bounds__(kFastThreads, 1)
+    paged_decode_fast(const __grid_constant__ CUtensorMap tmap, const FastParams p) {
+    using S = FastShape<D, HH, STAGES>;
+    constexpr int J = S::J;
+    constexpr int KS = D / 16;  // k-steps of QK^T
+    constexpr int NT = D / 8;   // n-tiles of the output
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStage);
+
+    const int seq = blockIdx.z;
+    const int hg = blockIdx.y;
+    const uint32_t split = blockIdx.x;
+    const int ctx = p.ctx[seq];
+    if (ctx <= 0 || static_cast<uint32_t>(ctx) > p.pitch * 16u) {
+        if (threadIdx.x == 0 && split == 0 && hg == 0) record_error(p.err, kErrBadContext);
+        return;
+    }
+    const uint32_t nblk_total = (static_cast<uint32_t>(ctx) + 15u) / 16u;
+    const uint32_t nsplits = (nblk_total + p.split_blocks - 1) / p.split_blocks;
+    if (nsplits > p.max_splits) {
+        if (threadIdx.x == 0 && split == 0 && hg == 0) record_error(p.err, kErrBadContext);
+        return;
+    }
+    const uint32_t b0 = split * p.split_blocks;
+    if (b0 >= nblk_total) return;
+    const uint32_t b1 = min(b0 + p.split_blocks, nblk_total);
+    const uint32_t nblk = b1 - b0;
+    const uint32_t iters = (nblk + J - 1) / J;
+
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + STAGES);
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, kFastComputeWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kFastComputeWarps) {
+        // Producer: one elected lane streams K and V slices of each block.
+        if (lane == 0) {
+            prefetch_tensormap(&tmap);
+            const uint64_t policy = l2_policy_evict_first();
+            const int32_t* row = p.tables + static_cast<size_t>(seq) * p.pitch;
+            for (uint32_t it = 0; it < iters; ++it) {
+                const uint32_t slot = it % STAGES;
+                if (it >= STAGES &&
+                    !mbar_wait_bounded(empty0 + 8 * slot, ((it / STAGES) - 1) & 1u)) {
+                    record_error(p.err, kErrWaitTimeout);
+                    break;
+                }
+                const uint32_t nb = min(static_cast<uint32_t>(J), nblk - it * J);
+                mbar_arrive_expect_tx(full0 + 8 * slot, nb * S::kBlock);
+                const uint32_t dst = smem_u32(smem + slot * S::kStage);
+                for (uint32_t j = 0; j < nb; ++j) {
+                    int32_t id = row[b0 + it * J + j];
+                    if (static_cast<uint32_t>(id) >= p.num_blocks) {
+                        record_error(p.err, kErrBadBlockId);
+                        id = 0;
+                    }
+                    const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
+                    tma_load_4d(dst + j * S::kBlock, &tmap, full0 + 8 * slot, 0, r, hg * HH, 0, policy);
+                    tma_load_4d(dst + j * S::kBlock + S::kBox, &tmap, full0 + 8 * slot, 0, r + 16,
+                                hg * HH, 0, policy);
+                }
+            }
+        }
+        return;
+    }
+
+    // Consumers: warp (hh, j) owns kv head hg*HH+hh and blocks j, j+J, ...
+    const int hh = warp % HH;
+    const int j = warp / HH;
+    const int kvh = hg * HH + hh;
+    const int g = lane >> 2;
+    const int c = lane & 3;
+    const int G = static_cast<int>(p.group);
+
+    // Query rows g and g+8 of the group as A fragments; rows >= G are zero.
+    uint32_t qa[KS][4];
+    {
+        const __nv_bfloat16* qb = p.q + (static_cast<size_t>(seq) * p.hq + static_cast<size_t>(kvh) * G) * D;
+        const uint32_t* q_lo = reinterpret_cast<const uint32_t*>(qb + g * D);
+        const uint32_t* q_hi = reinterpret_cast<const uint32_t*>(qb + (g + 8) * D);
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int k0 = (ks * 16 + c * 2) >> 1;
+            qa[ks][0] = (g < G) ? __ldg(q_lo + k0) : 0u;
+            qa[ks][1] = (g + 8 < G) ? __ldg(q_hi + k0) : 0u;
+            qa[ks][2] = (g < G) ? __ldg(q_lo + k0 + 4) : 0u;
+            qa[ks][3] = (g + 8 < G) ? __ldg(q_hi + k0 + 4) : 0u;
+        }
+    }
+
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    bool alive = true;
+
+    const int mi = lane >> 3;
+    const int li = lane & 7;
+
+    for (uint32_t it = 0; it < iters && alive; ++it) {
+        const uint32_t slot = it % STAGES;
+        if (!mbar_wait_bounded(full0 + 8 * slot, (it / STAGES) & 1u)) {
+            record_error(p.err, kErrWaitTimeout);
+            alive = false;
+            break;
+        }
+        const uint32_t lb = b0 + it * J + j;
+        if (lb < b1) {
+            const int valid = min(16, ctx - static_cast<int>(lb) * 16);
+            const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
+            const uint32_t vb = kb + S::kBox;
+
+            float s[2][4];
+#pragma unroll
+            for (int a = 0; a < 2; ++a) s[a][0] = s[a][1] = s[a][2] = s[a][3] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const int dh = ks >> 2;
+                const int chunk = ((ks & 3) << 1) + (mi & 1);
+                const int t = ((mi >> 1) << 3) + li;
+                uint32_t r0, r1, r2, r3;
+                ldmatrix_x4(box_addr(kb, dh * HH + hh, t, chunk), r0, r1, r2, r3);
+                mma_bf16_16816(s[0], qa[ks], r0, r1);
+                mma_bf16_16816(s[1], qa[ks], r2, r3);
+            }
+
+            // scale into the log2 domain and mask tokens past the context
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int tok = a * 8 + c * 2 + (e & 1);
+                    const float v = s[a][e] * p.scale_log2;
+                    s[a][e] = (tok < valid) ? v : -INFINITY;
+                }
+            }
+            float r_lo = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+            float r_hi = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+            r_lo = fmaxf(r_lo, __shfl_xor_sync(0xffffffffu, r_lo, 1));
+            r_lo = fmaxf(r_lo, __shfl_xor_sync(0xffffffffu, r_lo, 2));
+            r_hi = fmaxf(r_hi, __shfl_xor_sync(0xffffffffu, r_hi, 1));
+            r_hi = fmaxf(r_hi, __shfl_xor_sync(0xffffffffu, r_hi, 2));
+            const float mn0 = fmaxf(m0, r_lo);
+            const float mn1 = fmaxf(m1, r_hi);
+            const float corr0 = exp2f(m0 - mn0);
+            const float corr1 = exp2f(m1 - mn1);
+            m0 = mn0;
+            m1 = mn1;
+#pragma unroll
+            for (int a = 0; a < 2; ++a) {
+                s[a][0] = exp2f(s[a][0] - mn0);
+                s[a][1] = exp2f(s[a][1] - mn0);
+                s[a][2] = exp2f(s[a][2] - mn1);
+                s[a][3] = exp2f(s[a][3] - mn1);
+            }
+            l0 = l0 * corr0 + (s[0][0] + s[0][1] + s[1][0] + s[1][1]);
+            l1 = l1 * corr1 + (s[0][2] + s[0][3] + s[1][2] + s[1][3]);
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                o[n][0] *= corr0;
+                o[n][1] *= corr0;
+                o[n][2] *= corr1;
+                o[n][3] *= corr1;
+            }
+            const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
+                                    pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
+#pragma unroll
+            for (int np = 0; np < D / 16; ++np) {
+                const int dh = np >> 2;
+                const int chunk = ((np & 3) << 1) + (mi >> 1);
+                const int t = ((mi & 1) << 3) + li;
+                uint32_t v0, v1, v2, v3;
+                ldmatrix_x4_trans(box_addr(vb, dh * HH + hh, t, chunk), v0, v1, v2, v3);
+                if (valid < 16) {
+                    // V slots past the context may hold anything (even NaN);
+                    // zero them so the zero weights cannot turn them into NaN.
+                    v0 = mask_pair(v0, c * 2, valid);
+                    v2 = mask_pair(v2, c * 2, valid);
+                    v1 = mask_pair(v1, 8 + c * 2, valid);
+                    v3 = mask_pair(v3, 8 + c * 2, valid);
+                }
+                mma_bf16_16816(o[2 * np], pa, v0, v1);
+                mma_bf16_16816(o[2 * np + 1], pa, v2, v3);
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+    }
+
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+    // Merge the J warps that share a kv head through shared memory (the stage
+    // buffers are free once every consumer has passed the barrier).
+    if constexpr (J > 1) {
+        named_barrier(1, kFastComputeWarps * 32);
+        float* scratch = reinterpret_cast<float*>(smem);
+        constexpr int kSlot = 16 * D + 32;
+        if (j > 0) {
+            float* w = scratch + (hh * J + j) * kSlot;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const int col = n * 8 + c * 2;
+                *reinterpret_cast<float2*>(w + g * D + col) = make_float2(o[n][0], o[n][1]);
+                *reinterpret_cast<float2*>(w + (g + 8) * D + col) = make_float2(o[n][2], o[n][3]);
+            }
+            if (c == 0) {
+                w[16 * D + g] = m0;
+                w[16 * D + g + 8] = m1;
+                w[16 * D + 16 + g] = l0;
+                w[16 * D + 16 + g + 8] = l1;
+            }
+        }
+        named_barrier(1, kFastComputeWarps * 32);
+        if (j == 0) {
+            for (int jj = 1; jj < J; ++jj) {
+                const float* w = scratch + (hh * J + jj) * kSlot;
+                const float mj0 = w[16 * D + g], mj1 = w[16 * D + g + 8];
+                const float lj0 = w[16 * D + 16 + g], lj1 = w[16 * D + 16 + g + 8];
+                const float M0 = fmaxf(m0, mj0), M1 = fmaxf(m1, mj1);
+                const float a0 = exp2f(m0 - M0), a1 = exp2f(m1 - M1);
+                const float e0 = (mj0 == -INFINITY) ? 0.f : exp2f(mj0 - M0);
+                const float e1 = (mj1 == -INFINITY) ? 0.f : exp2f(mj1 - M1);
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    const int col = n * 8 + c * 2;
+                    const float2 lo = *reinterpret_cast<const float2*>(w + g * D + col);
+                    const float2 hi = *reinterpret_cast<const float2*>(w + (g + 8) * D + col);
+                    o[n][0] = o[n][0] * a0 + lo.x * e0;
+                    o[n][1] = o[n][1] * a0 + lo.y * e0;
+                    o[n][2] = o[n][2] * a1 + hi.x * e1;
+                    o[n][3] = o[n][3] * a1 + hi.y * e1;
+                }
+                l0 = l0 * a0 + lj0 * e0;
+                l1 = l1 * a1 + lj1 * e1;
+                m0 = M0;
+                m1 = M1;
+            }
+        }
+    }
+    if (j != 0 || !alive) return;
+
+    if (nsplits == 1) {
+        const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+        __nv_bfloat16* ob = p.out + (static_cast<size_t>(seq) * p.hq + static_cast<size_t>(kvh) * G) * D;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const int col = n * 8 + c * 2;
+            if (g < G)
+                *reinterpret_cast<uint32_t*>(ob + g * D + col) = pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
+            if (g + 8 < G)
+                *reinterpret_cast<uint32_t*>(ob + (g + 8) * D + col) =
+                    pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
+        }
+    } else {
+        const size_t part = (static_cast<size_t>(seq) * p.max_splits + split) * p.hq + static_cast<size_t>(kvh) * G;
+        float* wo = p.ws_o + part * D;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const int col = n * 8 + c * 2;
+            if (g < G) *reinterpret_cast<float2*>(wo + g * D + col) = make_float2(o[n][0], o[n][1]);
+            if (g + 8 < G) *reinterpret_cast<float2*>(wo + (g + 8) * D + col) = make_float2(o[n][2], o[n][3]);
+        }
+        if (c == 0) {
+            if (g < G) p.ws_ml[part + g] = make_float2(m0, l0);
+            if (g + 8 < G) p.ws_ml[part + g + 8] = make_float2(m1, l1);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+
+struct GenericParams {
+    const uint8_t* pool;
+    size_t block_stride;
+    const int32_t* tables;
+    const int32_t* ctx;
+    const void* q;
+    void* out;
+    float* ws_o;
+    float2* ws_ml;
+    int32_t* err;
+    uint32_t pitch;
+    uint32_t num_blocks;
+    uint32_t tokens_per_block;
+    uint32_t num_kv_heads;
+    uint32_t head_dim;
+    uint32_t layer;
+    uint32_t hq;
+    uint32_t group;
+    uint32_t split_tokens;
+    uint32_t max_splits;
+    float scale;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kGenericWarps * 32) paged_decode_generic(const GenericParams p) {
+    __shared__ float sm_ml[kGenericWarps][2];
+    __shared__ float sm_acc[kGenericWarps][kGenericMaxDimPerLane * 32];
+
+    const int seq = blockIdx.z;
+    const int qh = blockIdx.y;
+    const uint32_t split = blockIdx.x;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int ctx = p.ctx[seq];
+    if (ctx <= 0 || static_cast<uint32_t>(ctx) > p.pitch * p.tokens_per_block) {
+        if (threadIdx.x == 0 && split == 0 && qh == 0) record_error(p.err, kErrBadContext);
+        return;
+    }
+    const uint32_t nsplits = (static_cast<uint32_t>(ctx) + p.split_tokens - 1) / p.split_tokens;
+    if (nsplits > p.max_splits) {
+        if (threadIdx.x == 0 && split == 0 && qh == 0) record_error(p.err, kErrBadContext);
+        return;
+    }
+    const uint32_t t0 = split * p.split_tokens;
+    if (t0 >= static_cast<uint32_t>(ctx)) return;
+    const uint32_t t1 = min(t0 + p.split_tokens, static_cast<uint32_t>(ctx));
+
+    const uint32_t D = p.head_dim;
+    const uint32_t kvh = qh / p.group;
+    const T* q = static_cast<const T*>(p.q) + (static_cast<size_t>(seq) * p.hq + qh) * D;
+    float qr[kGenericMaxDimPerLane];
+    float acc[kGenericMaxDimPerLane];
+#pragma unroll
+    for (int i = 0; i < kGenericMaxDimPerLane; ++i) {
+        const uint32_t d = lane + 32 * i;
+        qr[i] = d < D ? to_float<T>(q[d]) : 0.f;
+        acc[i] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+
+    const size_t token_stride = static_cast<size_t>(p.num_kv_heads) * D;
+    const size_t stream_stride = token_stride * p.tokens_per_block;
+    const size_t layer_off = static_cast<size_t>(p.layer) * 2 * stream_stride + kvh * D;
+    const int32_t* row = p.tables + static_cast<size_t>(seq) * p.pitch;
+
+    for (uint32_t t = t0 + warp; t < t1; t += kGenericWarps) {
+        int32_t id = row[t / p.tokens_per_block];
+        if (static_cast<uint32_t>(id) >= p.num_blocks) {
+            if (lane == 0) record_error(p.err, kErrBadBlockId);
+            id = 0;
+        }
+        const T* kp = reinterpret_cast<const T*>(p.pool + static_cast<size_t>(id) * p.block_stride) +
+                      layer_off + (t % p.tokens_per_block) * token_stride;
+        const T* vp = kp + stream_stride;
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < kGenericMaxDimPerLane; ++i) {
+            const uint32_t d = lane + 32 * i;
+            if (d < D) dot += qr[i] * to_float<T>(kp[d]);
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+        const float s = dot * p.scale;
+        const float mn = fmaxf(m, s);
+        const float corr = expf(m - mn);
+        const float w = expf(s - mn);
+        l = l * corr + w;
+#pragma unroll
+        for (int i = 0; i < kGenericMaxDimPerLane; ++i) {
+            const uint32_t d = lane + 32 * i;
+            if (d < D) acc[i] = acc[i] * corr + w * to_float<T>(vp[d]);
+        }
+        m = mn;
+    }
+
+    if (lane == 0) {
+        sm_ml[warp][0] = m;
+        sm_ml[warp][1] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < kGenericMaxDimPerLane; ++i) sm_acc[warp][lane + 32 * i] = acc[i];
+    __syncthreads();
+    if (warp != 0) return;
+
+    float M = -INFINITY;
+    for (int w = 0; w < kGenericWarps; ++w) M = fmaxf(M, sm_ml[w][0]);
+    float L = 0.f;
+    float wt[kGenericWarps];
+    for (int w = 0; w < kGenericWarps; ++w) {
+        wt[w] = (sm_ml[w][0] == -INFINITY) ? 0.f : expf(sm_ml[w][0] - M);
+        L += wt[w] * sm_ml[w][1];
+    }
+    if (nsplits == 1) {
+        T* out = static_cast<T*>(p.out) + (static_cast<size_t>(seq) * p.hq + qh) * D;
+        for (uint32_t d = lane; d < D; d += 32) {
+            float a = 0.f;
+            for (int w = 0; w < kGenericWarps; ++w) a += wt[w] * sm_acc[w][d];
+            out[d] = from_float<T>(a / L);
+        }
+    } else {
+        const size_t part = (static_cast<size_t>(seq) * p.max_splits + split) * p.hq + qh;
+        float* wo = p.ws_o + part * D;
+        for (uint32_t d = lane; d < D; d += 32) {
+            float a = 0.f;
+            for (int w = 0; w < kGenericWarps; ++w) a += wt[w] * sm_acc[w][d];
+            wo[d] = a;
+        }
+        if (lane == 0) p.ws_ml[part] = make_float2(M, L);
+    }
+}
+
+// Merges the partitions of every (sequence, query head) whose context was
+// split. `log2_domain` says whether the partition maxima are base-2 (fast
+// kernel) or natural (generic kernel).
+template <typename T>
+__global__ void combine_partitions(const float* __restrict__ ws_o, const float2* __restrict__ ws_ml,
+                                   const int32_t* __restrict__ ctx_lens, T* __restrict__ out,
+                                   uint32_t hq, uint32_t D, uint32_t max_splits, uint32_t split_tokens,
+                                   int log2_domain) {
+    const int seq = blockIdx.y;
+    const int h = blockIdx.x;
+    const int ctx = ctx_lens[seq];
+    if (ctx <= 0) return;
+    const uint32_t ns = (static_cast<uint32_t>(ctx) + split_tokens - 1) / split_tokens;
+    if (ns <= 1 || ns > max_splits) return;
+    const size_t base = static_cast<size_t>(seq) * max_splits * hq + h;
+    float M = -INFINITY;
+    for (uint32_t s = 0; s < ns; ++s) M = fmaxf(M, ws_ml[base + s * hq].x);
+    float L = 0.f;
+    for (uint32_t s = 0; s < ns; ++s) {
+        const float2 ml = ws_ml[base + s * hq];
+        const float w = log2_domain ? exp2f(ml.x - M) : expf(ml.x - M);
+        L += w * ml.y;
+    }
+    const float inv = 1.f / L;
+    T* o = out + (static_cast<size_t>(seq) * hq + h) * D;
+    for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+        float a = 0.f;
+        for (uint32_t s = 0; s < ns; ++s) {
+            const float2 ml = ws_ml[base + s * hq];
+            const float w = log2_domain ? exp2f(ml.x - M) : expf(ml.x - M);
+            a += w * ws_o[(base + s * hq) * D + d];
+        }
+        o[d] = from_float<T>(a * inv);
+    }
+}
+
+// ---- host side ------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult qres;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
+                                             &qres) == cudaSuccess &&
+            qres == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        }
+    }
+    return fn;
+}
+
+// The pool viewed as a 4-D tensor of bf16 so one TMA box is the K (or V)
+// slice of one block for HH consecutive kv heads, laid out in shared memory
+// as [head_dim/64][HH][16 tokens][64]:
+//   dim0: 64 elements of head_dim        (contiguous)
+//   dim1: token rows of the whole pool   (stride kv_heads*head_dim*2 bytes)
+//   dim2: kv head                        (stride head_dim*2 bytes)
+//   dim3: 64-element half of head_dim    (stride 128 bytes)
+// Token row r of block b, layer l, stream s, slot t is ((b*L + l)*2 + s)*16 + t,
+// which needs blocks stored back to back (stride == byte_size).
+int encode_pool_map(const qvp_decode_args& a, uint32_t hh, CUtensorMap* map) {
+    struct Key {
+        const void* pool;
+        uint32_t num_blocks, layers, heads, dim, hh;
+    };
+    static thread_local Key last{};
+    static thread_local CUtensorMap cached;
+    const Key key{a.pool, a.num_blocks, a.shape.num_layers, a.shape.num_kv_heads, a.shape.head_dim, hh};
+    if (std::memcmp(&key, &last, sizeof(Key)) == 0) {
+        *map = cached;
+        return QVP_OK;
+    }
+    auto encode = get_encode_fn();
+    if (encode == nullptr) return fail(QVP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    const uint32_t D = a.shape.head_dim;
+    const uint32_t H = a.shape.num_kv_heads;
+    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(a.num_blocks) * a.shape.num_layers * 2 * 16, H, D / 64};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(H) * D * 2, static_cast<cuuint64_t>(D) * 2, 128};
+    cuuint32_t box[4] = {64, 16, hh, D / 64};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.pool), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(QVP_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
+    last = key;
+    cached = *map;
+    return QVP_OK;
+}
+
+template <int D, int HH, int STAGES>
+int launch_fast_t(const qvp_decode_args& a, const DecodePlan& plan, const FastParams& fp, cudaStream_t st) {
+    using S = FastShape<D, HH, STAGES>;
+    static bool attr_set = false;
+    auto kern = paged_decode_fast<D, HH, STAGES>;
+    if (!attr_set) {
+        int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
+                            "cudaFuncSetAttribute(fast decode)");
+        if (rc != QVP_OK) return rc;
+        attr_set = true;
+    }
+    CUtensorMap map;
+    int rc = encode_pool_map(a, HH, &map);
+    if (rc != QVP_OK) return rc;
+    dim3 grid(plan.max_splits, a.shape.num_kv_heads / HH, a.batch);
+    kern<<<grid, kFastThreads, S::kSmem, st>>>(map, fp);
+    return check_cuda(cudaGetLastError(), "launch fast decode");
+}
+
+int launch_fast(const qvp_decode_args& a, const DecodePlan& plan, const FastParams& fp, cudaStream_t st) {
+    const uint32_t D = a.shape.head_dim;
+    switch (plan.heads_per_cta) {
+        case 4: return D == 128 ? launch_fast_t<128, 4, 3>(a, plan, fp, st) : launch_fast_t<64, 4, 6>(a, plan, fp, st);
+        case 2: return D == 128 ? launch_fast_t<128, 2, 3>(a, plan, fp, st) : launch_fast_t<64, 2, 6>(a, plan, fp, st);
+        default: return D == 128 ? launch_fast_t<128, 1, 3>(a, plan, fp, st) : launch_fast_t<64, 1, 6>(a, plan, fp, st);
+    }
+}
+
+}  // namespace
+
+int plan_decode(const qvp_decode_args& a, DecodePlan& plan) {
+    plan = DecodePlan{};
+    const qvp_block_shape& sh = a.shape;
+    if (sh.tokens_per_block == 0 || sh.num_layers == 0 || sh.num_kv_heads == 0 || sh.head_dim == 0)
+        return fail(QVP_ERR_INVALID, "block shape has a zero field");
+    const uint32_t elem = a.dtype == QVP_DTYPE_F32 ? 4u : a.dtype == QVP_DTYPE_BF16 ? 2u : 0u;
+    if (elem == 0) return fail(QVP_ERR_INVALID, "unknown dtype %d", a.dtype);
+    if (sh.bytes_per_element != elem)
+        return fail(QVP_ERR_INVALID, "bytes_per_element %u does not match the dtype", sh.bytes_per_element);
+    if (a.layer >= sh.num_layers) return fail(QVP_ERR_INVALID, "layer %u >= num_layers %u", a.layer, sh.num_layers);
+    if (a.num_query_heads == 0 || a.num_query_heads % sh.num_kv_heads != 0)
+        return fail(QVP_ERR_INVALID, "num_query_heads %u is not a positive multiple of num_kv_heads %u",
+                    a.num_query_heads, sh.num_kv_heads);
+    if (a.batch == 0) return QVP_OK;
+    if (a.pool == nullptr || a.block_tables == nullptr || a.context_lens == nullptr || a.query == nullptr ||
+        a.out == nullptr)
+        return fail(QVP_ERR_INVALID, "null pool, table, context, query or output pointer");
+    if (a.batch > 65535 || a.num_query_heads > 65535) return fail(QVP_ERR_UNSUPPORTED, "batch or heads above 65535");
+    const size_t block_bytes = qvp_block_bytes(&sh);
+    if (a.block_stride < block_bytes) return fail(QVP_ERR_INVALID, "block_stride below the block size");
+    if (a.num_blocks == 0) return fail(QVP_ERR_INVALID, "empty pool");
+    if (a.max_context_len == 0) return fail(QVP_ERR_INVALID, "max_context_len is zero");
+    if (static_cast<uint64_t>(a.max_context_len) >
+        static_cast<uint64_t>(a.max_blocks_per_seq) * sh.tokens_per_block)
+        return fail(QVP_ERR_INVALID, "max_context_len exceeds the table capacity");
+    if (sh.head_dim > 32u * kGenericMaxDimPerLane)
+        return fail(QVP_ERR_UNSUPPORTED, "head_dim %u above 256", sh.head_dim);
+
+    plan.group = a.num_query_heads / sh.num_kv_heads;
+    const uintptr_t pool_addr = reinterpret_cast<uintptr_t>(a.pool);
+    plan.fast = a.dtype == QVP_DTYPE_BF16 && sh.tokens_per_block == 16 &&
+                (sh.head_dim == 64 || sh.head_dim == 128) && plan.group <= 16 &&
+                a.block_stride == block_bytes && (pool_addr & 15u) == 0 &&
+                (reinterpret_cast<uintptr_t>(a.query) & 3u) == 0 &&
+                (reinterpret_cast<uintptr_t>(a.out) & 3u) == 0 && sh.num_kv_heads <= 256 &&
+                static_cast<uint64_t>(a.num_blocks) * sh.num_layers * 32u < (1ull << 31);
+    plan.heads_per_cta = sh.num_kv_heads % 4 == 0 ? 4 : sh.num_kv_heads % 2 == 0 ? 2 : 1;
+
+    uint32_t split = a.split_tokens;
+    if (split != 0) {
+        if (plan.fast && split % 16 != 0)
+            return fail(QVP_ERR_INVALID, "split_tokens %u is not a multiple of 16", split);
+    } else {
+        // Smallest power-of-two partition (>= 256 tokens) that keeps the grid
+        // of the longest context within about eight CTAs per SM.
+        const uint32_t ctas_per_part = plan.fast ? sh.num_kv_heads / plan.heads_per_cta : a.num_query_heads;
+        const uint64_t target = 8ull * static_cast<uint64_t>(device_sm_count() > 0 ? device_sm_count() : 148);
+        split = 256;
+        while (static_cast<uint64_t>(a.batch) * ctas_per_part * ceil_div(a.max_context_len, split) > target &&
+               split < a.max_context_len)
+            split *= 2;
+    }
+    plan.split_tokens = split;
+    plan.max_splits = ceil_div(a.max_context_len, split);
+    if (plan.max_splits > 0x7fffffffu) return fail(QVP_ERR_UNSUPPORTED, "too many partitions");
+    if (plan.max_splits > 1) {
+        const size_t parts = static_cast<size_t>(a.batch) * plan.max_splits * a.num_query_heads;
+        plan.workspace_bytes = round_up(parts * sh.head_dim * sizeof(float), 256) + parts * sizeof(float2);
+    }
+    return QVP_OK;
+}
+
+}  // namespace qvp
+
+using namespace qvp;
+
+extern "C" int qvp_decode_workspace_size(const qvp_decode_args* args, size_t* bytes) {
+    if (args == nullptr || bytes == nullptr) return fail(QVP_ERR_INVALID, "null argument");
+    DecodePlan plan;
+    const int rc = plan_decode(*args, plan);
+    if (rc != QVP_OK) return rc;
+    *bytes = plan.workspace_bytes;
+    return QVP_OK;
+}
+
+extern "C" int qvp_decode_plan(const qvp_decode_args* args, uint32_t* split_tokens, uint32_t* num_splits,
+                               int* fast_path) {
+    if (args == nullptr) return fail(QVP_ERR_INVALID, "null argument");
+    DecodePlan plan;
+    const int rc = plan_decode(*args, plan);
+    if (rc != QVP_OK) return rc;
+    if (split_tokens) *split_tokens = plan.split_tokens;
+    if (num_splits) *num_splits = plan.max_splits;
+    if (fast_path) *fast_path = plan.fast ? 1 : 0;
+    return QVP_OK;
+}
+
+extern "C" int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream) {
+    if (args == nullptr) return fail(QVP_ERR_INVALID, "null argument");
+    const qvp_decode_args& a = *args;
+    DecodePlan plan;
+    int rc = plan_decode(a, plan);
+    if (rc != QVP_OK || a.batch == 0) return rc;
+    if (plan.workspace_bytes > 0 && (a.workspace == nullptr || a.workspace_bytes < plan.workspace_bytes))
+        return fail(QVP_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", plan.workspace_bytes,
+                    a.workspace == nullptr ? size_t(0) : a.workspace_bytes);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const size_t parts = static_cast<size_t>(a.batch) * plan.max_splits * a.num_query_heads;
+    float* ws_o = static_cast<float*>(a.workspace);
+    float2* ws_ml = plan.workspace_bytes
+                        ? reinterpret_cast<float2*>(static_cast<uint8_t*>(a.workspace) +
+                                                    round_up(parts * a.shape.head_dim * sizeof(float), 256))
+                        : nullptr;
+    const uint32_t D = a.shape.head_dim;
+
+    if (plan.fast) {
+        FastParams fp;
+        fp.tables = a.block_tables;
+        fp.ctx = a.context_lens;
+        fp.q = static_cast<const __nv_bfloat16*>(a.query);
+        fp.out = static_cast<__nv_bfloat16*>(a.out);
+        fp.ws_o = ws_o;
+        fp.ws_ml = ws_ml;
+        fp.err = a.error_word;
+        fp.pitch = a.max_blocks_per_seq;
+        fp.num_blocks = a.num_blocks;
+        fp.layer = a.layer;
+        fp.num_layers = a.shape.num_layers;
+        fp.hq = a.num_query_heads;
+        fp.group = plan.group;
+        fp.split_blocks = plan.split_tokens / 16;
+        fp.max_splits = plan.max_splits;
+        fp.scale_log2 = a.scale * 1.4426950408889634f;  // log2(e)
+        rc = launch_fast(a, plan, fp, st);
+    } else {
+        GenericParams gp;
+        gp.pool = static_cast<const uint8_t*>(a.pool);
+        gp.block_stride = a.block_stride;
+        gp.tables = a.block_tables;
+        gp.ctx = a.context_lens;
+        gp.q = a.query;
+        gp.out = a.out;
+        gp.ws_o = ws_o;
+        gp.ws_ml = ws_ml;
+        gp.err = a.error_word;
+        gp.pitch = a.max_blocks_per_seq;
+        gp.num_blocks = a.num_blocks;
+        gp.tokens_per_block = a.shape.tokens_per_block;
+        gp.num_kv_heads = a.shape.num_kv_heads;
+        gp.head_dim = D;
+        gp.layer = a.layer;
+        gp.hq = a.num_query_heads;
+        gp.group = plan.group;
+        gp.split_tokens = plan.split_tokens;
+        gp.max_splits = plan.max_splits;
+        gp.scale = a.scale;
+        dim3 grid(plan.max_splits, a.num_query_heads, a.batch);
+        if (a.dtype == QVP_DTYPE_F32)
+            paged_decode_generic<float><<<grid, kGenericWarps * 32, 0, st>>>(gp);
+        else
+            paged_decode_generic<__nv_bfloat16><<<grid, kGenericWarps * 32, 0, st>>>(gp);
+        rc = check_cuda(cudaGetLastError(), "launch generic decode");
+    }
+    if (rc != QVP_OK || plan.max_splits <= 1) return rc;
+
+    dim3 grid(a.num_query_heads, a.batch);
+    const int threads = D >= 128 ? 128 : 64;
+    const int log2_domain = plan.fast ? 1 : 0;
+    if (a.dtype == QVP_DTYPE_F32)
+        combine_partitions<float><<<grid, threads, 0, st>>>(ws_o, ws_ml, a.context_lens, static_cast<float*>(a.out),
+                                                            a.num_query_heads, D, plan.max_splits,
+                                                            plan.split_tokens, log2_domain);
+    else
+        combine_partitions<__nv_bfloat16><<<grid, threads, 0, st>>>(
+            ws_o, ws_ml, a.context_lens, static_cast<__nv_bfloat16*>(a.out), a.num_query_heads, D,
+            plan.max_splits, plan.split_tokens, log2_domain);
+    return check_cuda(cudaGetLastError(), "launch combine");
+}

@@ -1,0 +1,39 @@
+// Host-side internals shared by the qvp translation units: error text,
+// CUDA status checks, the decode plan.
+#pragma once
+
+#include "qvp.h"
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+
+namespace qvp {
+
+// Stores printf-style text as this thread's last error and returns `status`.
+int fail(int status, const char* fmt, ...);
+// Returns QVP_OK, or QVP_ERR_CUDA with `what` and the CUDA error text recorded.
+int check_cuda(cudaError_t err, const char* what);
+
+inline bool is_pow2(uint32_t v) { return v != 0 && (v & (v - 1)) == 0; }
+inline size_t round_up(size_t v, size_t a) { return a == 0 ? v : (v + a - 1) / a * a; }
+inline uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
+
+// What one qvp_decode call will launch.
+struct DecodePlan {
+    bool fast = false;          // TMA + tensor-core kernel (bf16, D 64/128, 16-token blocks)
+    uint32_t group = 0;         // query heads per kv head (G)
+    uint32_t heads_per_cta = 0; // kv heads one fast CTA owns (HH)
+    uint32_t split_tokens = 0;  // tokens per split-K partition
+    uint32_t max_splits = 0;    // partitions of the longest context
+    size_t workspace_bytes = 0; // 0 when max_splits == 1
+};
+
+// Validates `a` and fills `plan`; returns a qvp_status.
+int plan_decode(const qvp_decode_args& a, DecodePlan& plan);
+
+int device_sm_count();
+
+}  // namespace qvp
