@@ -204,7 +204,7 @@ def run_ours(args):
     total_ms = timed(step, args.steps)
     # Clocks: the timed region of a short run can be shorter than the sampling
     # period, so keep the same step running untimed until ~1 s has elapsed.
-    t_end = time.time() + 1.0
+    t_end = time.time() + (0.0 if args.profile else 1.0)
     while time.time() < t_end:
         for _ in range(50):
             step()
@@ -235,15 +235,17 @@ def run_ours(args):
         step()
         out_h.copy_(out, non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize()
-    e2e_ms = timed(e2e_step, args.steps) / args.steps
+    e2e_ms = float("nan")
+    if not args.profile:
+        for _ in range(args.warmup):
+            e2e_step()
+        torch.cuda.synchronize()
+        e2e_ms = timed(e2e_step, args.steps) / args.steps
     h2d = q.numel() * q.element_size() + w.tables.nbytes + w.context_lens.nbytes
     d2h = out.numel() * out.element_size()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not (args.no_cpu or args.profile):
         host_pool = pool.view(torch.uint8).cpu().numpy() if w.elem == 2 else pool.cpu().numpy().view(np.uint8)
         host_q = q.cpu().view(torch.int16).numpy().view(np.uint16) if w.dtype == "bf16" else q.cpu().numpy()
         cpu = cpu_baseline(w, host_pool.reshape(-1), host_q, budget_s=args.cpu_budget)
@@ -429,6 +431,8 @@ def main():
     p.add_argument("--split", type=int, default=0, help="split-K partition in tokens (0 = auto)")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--profile", action="store_true",
+                   help="for ncu: only warm-up and timed decode steps (no clock probe, e2e or CPU baseline)")
     args = p.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -152,6 +152,17 @@ def small(seed: int, *, batch: int, ctx_lo: int, ctx_hi: int, hq: int, hkv: int,
                           layer=layer)
 
 
+def with_contexts(w: DecodeWorkload, context_lens) -> DecodeWorkload:
+    """The same workload with new context lengths and tables re-drawn for them."""
+    rng = np.random.default_rng(w.seed + 77)
+    ctx = np.asarray(context_lens, dtype=np.int32)
+    used = int(np.ceil(ctx / w.tokens_per_block).sum())
+    num_blocks = max(w.num_blocks, used)
+    tables = scattered_tables(rng, ctx, w.tokens_per_block, num_blocks)
+    return DecodeWorkload(w.name, w.tokens_per_block, w.num_layers, w.num_kv_heads, w.head_dim, w.dtype,
+                          w.num_query_heads, w.scale, ctx, tables, num_blocks, w.seed, layer=w.layer)
+
+
 def host_inputs(w: DecodeWorkload, seed_offset: int = 1000):
     """(pool bytes as uint8 [num_blocks*stride], query array) in the workload dtype.
 

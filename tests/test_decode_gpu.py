@@ -68,7 +68,9 @@ def test_bf16_fast_path_split_k(split):
 
 def test_bf16_fast_path_partial_last_blocks_and_tiny_contexts():
     w = W.small(8, batch=12, ctx_lo=1, ctx_hi=40, hq=28, hkv=4, head_dim=128, dtype="bf16")
-    w.context_lens[:4] = [1, 15, 16, 17]
+    ctx = w.context_lens.copy()
+    ctx[:4] = [1, 15, 16, 17]
+    w = W.with_contexts(w, ctx)
     check(w, expect_fast=True)
 
 
@@ -76,7 +78,7 @@ def test_bf16_padded_slots_hold_nan_without_leaking():
     # slots past each context inside the last block hold NaN; the kernel
     # must neither read them into the softmax nor let 0 * NaN reach out
     w = W.small(9, batch=4, ctx_lo=3, ctx_hi=60, hq=28, hkv=4, head_dim=128, dtype="bf16")
-    w.context_lens[:] = [3, 17, 33, 60]
+    w = W.with_contexts(w, [3, 17, 33, 60])
     pool, q = W.host_inputs(w)
     poolv = pool.reshape(w.num_blocks, w.block_stride)
     row = w.num_kv_heads * w.head_dim * 2
