@@ -166,7 +166,10 @@ def run_ours(args):
         a.workspace_bytes = plan["workspace_bytes"]
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
-    launches_per_step = 1 + (1 if plan["num_splits"] > 1 else 0)
+    launches_per_step = 2 if plan["stream"] else 1 + (1 if plan["num_splits"] > 1 else 0)
+    kernel_name = ("paged_decode_stream (persistent stream-K, TMA + mma.sync) + combine_records" if plan["stream"]
+                   else "paged_decode_fast (grid split-K, TMA + mma.sync) + combine_partitions" if plan["fast"]
+                   else "paged_decode_generic + combine_partitions")
 
     def step():
         st = qvp.decode(a, sh)
@@ -277,7 +280,7 @@ def run_ours(args):
                 "pool_blocks": w.num_blocks,
                 "split_tokens": plan["split_tokens"],
                 "num_splits_max": plan["num_splits"],
-                "kernel": "paged_decode_fast (TMA + mma.sync)" if plan["fast"] else "paged_decode_generic",
+                "kernel": kernel_name,
                 "l2": f"inputs larger than L2 ({w.kv_bytes() / 1e6:.0f} MB of K/V read per step)",
                 "parallelism": f"dp{world}" if scaling == "weak" else f"kv-head shards x{world}",
             },
@@ -291,7 +294,7 @@ def run_ours(args):
                 "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                 else "fallback 6.65 TB/s",
                 "traffic": traffic,
-                "kernel": "decode step = paged_decode_fast + combine_partitions, CUDA events, mean over steps",
+                "kernel": f"decode step = {kernel_name}, CUDA events, mean over steps",
                 "algorithmic_bytes_per_step": alg,
             },
             "e2e": {

@@ -81,6 +81,124 @@ __device__ __forceinline__ uint32_t mask_pair(uint32_t x, int t0, int valid) {
     return x & (lo | hi);
 }
 
+// Online-softmax state of one consumer warp: query rows g and g+8 of its
+// GQA group (row max in the log2 domain, lane-partial row sums) and the
+// m16n8 accumulator fragments of out[16][D].
+template <int D>
+struct WarpState {
+    float o[D / 8][4];
+    float m0, m1, l0, l1;
+
+    __device__ __forceinline__ void reset() {
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
+    }
+};
+
+// Query rows g and g+8 of the group that reads kv head `kvh` of sequence
+// `seq`, as m16n8k16 A fragments; rows >= G are zero.
+template <int D>
+__device__ __forceinline__ void load_query_fragments(uint32_t (&qa)[D / 16][4], const __nv_bfloat16* q, int seq,
+                                                     uint32_t hq, int kvh, int G, int lane) {
+    const int g = lane >> 2, c = lane & 3;
+    const __nv_bfloat16* qb = q + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kvh) * G) * D;
+    const uint32_t* q_lo = reinterpret_cast<const uint32_t*>(qb + g * D);
+    const uint32_t* q_hi = reinterpret_cast<const uint32_t*>(qb + (g + 8) * D);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+        const int k0 = (ks * 16 + c * 2) >> 1;
+        qa[ks][0] = (g < G) ? __ldg(q_lo + k0) : 0u;
+        qa[ks][1] = (g + 8 < G) ? __ldg(q_hi + k0) : 0u;
+        qa[ks][2] = (g < G) ? __ldg(q_lo + k0 + 4) : 0u;
+        qa[ks][3] = (g + 8 < G) ? __ldg(q_hi + k0 + 4) : 0u;
+    }
+}
+
+// One 16-token block of one kv head: S = Q K^T on tensor cores, masked to the
+// `valid` leading tokens, online-softmax update, O += P V. `kb` and `vb` are
+// the shared-memory boxes of K and V holding HH heads; `row_head` picks the
+// head inside them.
+template <int D, int HH>
+__device__ __forceinline__ void attend_block(WarpState<D>& st, const uint32_t (&qa)[D / 16][4], uint32_t kb,
+                                             uint32_t vb, int row_head, int valid, float scale_log2, int lane) {
+    const int c = lane & 3;
+    const int mi = lane >> 3;
+    const int li = lane & 7;
+    float s[2][4];
+#pragma unroll
+    for (int a = 0; a < 2; ++a) s[a][0] = s[a][1] = s[a][2] = s[a][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+        const int dh = ks >> 2;
+        const int chunk = ((ks & 3) << 1) + (mi & 1);
+        const int t = ((mi >> 1) << 3) + li;
+        uint32_t r0, r1, r2, r3;
+        ldmatrix_x4(box_addr(kb, dh * HH + row_head, t, chunk), r0, r1, r2, r3);
+        mma_bf16_16816(s[0], qa[ks], r0, r1);
+        mma_bf16_16816(s[1], qa[ks], r2, r3);
+    }
+    // scale into the log2 domain and mask tokens past the context
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int tok = a * 8 + c * 2 + (e & 1);
+            const float v = s[a][e] * scale_log2;
+            s[a][e] = (tok < valid) ? v : -INFINITY;
+        }
+    }
+    float r_lo = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
+    float r_hi = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
+    r_lo = fmaxf(r_lo, __shfl_xor_sync(0xffffffffu, r_lo, 1));
+    r_lo = fmaxf(r_lo, __shfl_xor_sync(0xffffffffu, r_lo, 2));
+    r_hi = fmaxf(r_hi, __shfl_xor_sync(0xffffffffu, r_hi, 1));
+    r_hi = fmaxf(r_hi, __shfl_xor_sync(0xffffffffu, r_hi, 2));
+    const float mn0 = fmaxf(st.m0, r_lo);
+    const float mn1 = fmaxf(st.m1, r_hi);
+    const float corr0 = exp2f(st.m0 - mn0);
+    const float corr1 = exp2f(st.m1 - mn1);
+    st.m0 = mn0;
+    st.m1 = mn1;
+#pragma unroll
+    for (int a = 0; a < 2; ++a) {
+        s[a][0] = exp2f(s[a][0] - mn0);
+        s[a][1] = exp2f(s[a][1] - mn0);
+        s[a][2] = exp2f(s[a][2] - mn1);
+        s[a][3] = exp2f(s[a][3] - mn1);
+    }
+    st.l0 = st.l0 * corr0 + (s[0][0] + s[0][1] + s[1][0] + s[1][1]);
+    st.l1 = st.l1 * corr1 + (s[0][2] + s[0][3] + s[1][2] + s[1][3]);
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+        st.o[n][0] *= corr0;
+        st.o[n][1] *= corr0;
+        st.o[n][2] *= corr1;
+        st.o[n][3] *= corr1;
+    }
+    const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
+                            pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
+#pragma unroll
+    for (int np = 0; np < D / 16; ++np) {
+        const int dh = np >> 2;
+        const int chunk = ((np & 3) << 1) + (mi >> 1);
+        const int t = ((mi & 1) << 3) + li;
+        uint32_t v0, v1, v2, v3;
+        ldmatrix_x4_trans(box_addr(vb, dh * HH + row_head, t, chunk), v0, v1, v2, v3);
+        if (valid < 16) {
+            // V slots past the context may hold anything (even NaN); zero them
+            // so the zero weights cannot turn them into NaN.
+            v0 = mask_pair(v0, c * 2, valid);
+            v2 = mask_pair(v2, c * 2, valid);
+            v1 = mask_pair(v1, 8 + c * 2, valid);
+            v3 = mask_pair(v3, 8 + c * 2, valid);
+        }
+        mma_bf16_16816(st.o[2 * np], pa, v0, v1);
+        mma_bf16_16816(st.o[2 * np + 1], pa, v2, v3);
+    }
+}
+
 template <int D, int HH, int STAGES>
 __global__ void __launch_bounds__(kFastThreads, 1)
     paged_decode_fast(const __grid_constant__ CUtensorMap tmap, const FastParams p) {
@@ -168,30 +286,11 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     const int c = lane & 3;
     const int G = static_cast<int>(p.group);
 
-    // Query rows g and g+8 of the group as A fragments; rows >= G are zero.
     uint32_t qa[KS][4];
-    {
-        const __nv_bfloat16* qb = p.q + (static_cast<size_t>(seq) * p.hq + static_cast<size_t>(kvh) * G) * D;
-        const uint32_t* q_lo = reinterpret_cast<const uint32_t*>(qb + g * D);
-        const uint32_t* q_hi = reinterpret_cast<const uint32_t*>(qb + (g + 8) * D);
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            const int k0 = (ks * 16 + c * 2) >> 1;
-            qa[ks][0] = (g < G) ? __ldg(q_lo + k0) : 0u;
-            qa[ks][1] = (g + 8 < G) ? __ldg(q_hi + k0) : 0u;
-            qa[ks][2] = (g < G) ? __ldg(q_lo + k0 + 4) : 0u;
-            qa[ks][3] = (g + 8 < G) ? __ldg(q_hi + k0 + 4) : 0u;
-        }
-    }
-
-    float o[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    load_query_fragments<D>(qa, p.q, seq, p.hq, kvh, G, lane);
+    WarpState<D> st;
+    st.reset();
     bool alive = true;
-
-    const int mi = lane >> 3;
-    const int li = lane & 7;
 
     for (uint32_t it = 0; it < iters && alive; ++it) {
         const uint32_t slot = it % STAGES;
@@ -204,84 +303,13 @@ __global__ void __launch_bounds__(kFastThreads, 1)
         if (lb < b1) {
             const int valid = min(16, ctx - static_cast<int>(lb) * 16);
             const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
-            const uint32_t vb = kb + S::kBox;
-
-            float s[2][4];
-#pragma unroll
-            for (int a = 0; a < 2; ++a) s[a][0] = s[a][1] = s[a][2] = s[a][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                const int dh = ks >> 2;
-                const int chunk = ((ks & 3) << 1) + (mi & 1);
-                const int t = ((mi >> 1) << 3) + li;
-                uint32_t r0, r1, r2, r3;
-                ldmatrix_x4(box_addr(kb, dh * HH + hh, t, chunk), r0, r1, r2, r3);
-                mma_bf16_16816(s[0], qa[ks], r0, r1);
-                mma_bf16_16816(s[1], qa[ks], r2, r3);
-            }
-
-            // scale into the log2 domain and mask tokens past the context
-#pragma unroll
-            for (int a = 0; a < 2; ++a) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int tok = a * 8 + c * 2 + (e & 1);
-                    const float v = s[a][e] * p.scale_log2;
-                    s[a][e] = (tok < valid) ? v : -INFINITY;
-                }
-            }
-            float r_lo = fmaxf(fmaxf(s[0][0], s[0][1]), fmaxf(s[1][0], s[1][1]));
-            float r_hi = fmaxf(fmaxf(s[0][2], s[0][3]), fmaxf(s[1][2], s[1][3]));
-            r_lo = fmaxf(r_lo, __shfl_xor_sync(0xffffffffu, r_lo, 1));
-            r_lo = fmaxf(r_lo, __shfl_xor_sync(0xffffffffu, r_lo, 2));
-            r_hi = fmaxf(r_hi, __shfl_xor_sync(0xffffffffu, r_hi, 1));
-            r_hi = fmaxf(r_hi, __shfl_xor_sync(0xffffffffu, r_hi, 2));
-            const float mn0 = fmaxf(m0, r_lo);
-            const float mn1 = fmaxf(m1, r_hi);
-            const float corr0 = exp2f(m0 - mn0);
-            const float corr1 = exp2f(m1 - mn1);
-            m0 = mn0;
-            m1 = mn1;
-#pragma unroll
-            for (int a = 0; a < 2; ++a) {
-                s[a][0] = exp2f(s[a][0] - mn0);
-                s[a][1] = exp2f(s[a][1] - mn0);
-                s[a][2] = exp2f(s[a][2] - mn1);
-                s[a][3] = exp2f(s[a][3] - mn1);
-            }
-            l0 = l0 * corr0 + (s[0][0] + s[0][1] + s[1][0] + s[1][1]);
-            l1 = l1 * corr1 + (s[0][2] + s[0][3] + s[1][2] + s[1][3]);
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                o[n][0] *= corr0;
-                o[n][1] *= corr0;
-                o[n][2] *= corr1;
-                o[n][3] *= corr1;
-            }
-            const uint32_t pa[4] = {pack_bf16x2(s[0][0], s[0][1]), pack_bf16x2(s[0][2], s[0][3]),
-                                    pack_bf16x2(s[1][0], s[1][1]), pack_bf16x2(s[1][2], s[1][3])};
-#pragma unroll
-            for (int np = 0; np < D / 16; ++np) {
-                const int dh = np >> 2;
-                const int chunk = ((np & 3) << 1) + (mi >> 1);
-                const int t = ((mi & 1) << 3) + li;
-                uint32_t v0, v1, v2, v3;
-                ldmatrix_x4_trans(box_addr(vb, dh * HH + hh, t, chunk), v0, v1, v2, v3);
-                if (valid < 16) {
-                    // V slots past the context may hold anything (even NaN);
-                    // zero them so the zero weights cannot turn them into NaN.
-                    v0 = mask_pair(v0, c * 2, valid);
-                    v2 = mask_pair(v2, c * 2, valid);
-                    v1 = mask_pair(v1, 8 + c * 2, valid);
-                    v3 = mask_pair(v3, 8 + c * 2, valid);
-                }
-                mma_bf16_16816(o[2 * np], pa, v0, v1);
-                mma_bf16_16816(o[2 * np + 1], pa, v2, v3);
-            }
+            attend_block<D, HH>(st, qa, kb, kb + S::kBox, hh, valid, p.scale_log2, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * slot);
     }
+    float m0 = st.m0, m1 = st.m1, l0 = st.l0, l1 = st.l1;
+    auto& o = st.o;
 
     l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
@@ -362,6 +390,395 @@ __global__ void __launch_bounds__(kFastThreads, 1)
         if (c == 0) {
             if (g < G) p.ws_ml[part + g] = make_float2(m0, l0);
             if (g + 8 < G) p.ws_ml[part + g + 8] = make_float2(m1, l1);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent stream-K variant of the fast kernel.
+//
+// A "segment" is one (sequence, head group) pair; its blocks are cut into
+// stages of J blocks (the last stage of a segment may be short). All stages of
+// all segments, in sequence order, form one stream that is split evenly over
+// a grid of one CTA per SM: CTA c owns stages [c*S/grid, (c+1)*S/grid). The
+// producer warp walks that range streaming K/V with TMA, crossing segment
+// boundaries without a pause; every consumer warp keeps one running (max, sum,
+// accumulator) per segment piece and writes it as a partial record when the
+// piece ends. Records of segment sigma written by CTA c live at index
+// sigma + c, which is injective because segments and CTA ranges are both
+// contiguous in stage order. `combine_records`, launched as a programmatic
+// dependent (already resident when the decode grid drains), merges them.
+
+constexpr int kStreamMaxSegments = 4096;
+
+struct StreamParams {
+    const int32_t* tables;
+    const int32_t* ctx;
+    const __nv_bfloat16* q;
+    float* rec_acc;       // [records][G][D]
+    float2* rec_ml;       // [records][G]
+    int32_t* seg_prefix;  // [nseg + 1] stage prefix, written by CTA 0 for the combine
+    int32_t* err;
+    uint32_t pitch;
+    uint32_t num_blocks;
+    uint32_t layer;
+    uint32_t num_layers;
+    uint32_t hq;
+    uint32_t group;
+    uint32_t head_groups;  // z = kv heads / HH
+    uint32_t nseg;         // batch * z
+    float scale_log2;
+};
+
+__device__ __forceinline__ void grid_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+__device__ __forceinline__ void grid_dependency_wait() {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// True when CTA `cta` of a `grid`-CTA stream-K launch over `total` stages
+// got an empty range (possible when total < grid); such a CTA wrote nothing.
+__device__ __forceinline__ bool cta_is_empty(uint32_t cta, uint32_t total, uint32_t grid) {
+    return static_cast<uint64_t>(cta) * total / grid == static_cast<uint64_t>(cta + 1) * total / grid;
+}
+
+// Largest sigma in [0, nseg) with prefix[sigma] <= x (prefix non-decreasing).
+__device__ __forceinline__ int find_segment(const int32_t* prefix, int nseg, uint32_t x) {
+    int lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (static_cast<uint32_t>(prefix[mid]) <= x)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+template <int D, int HH, int STAGES>
+__global__ void __launch_bounds__(kFastThreads, 1)
+    paged_decode_stream(const __grid_constant__ CUtensorMap tmap, const StreamParams p) {
+    using S = FastShape<D, HH, STAGES>;
+    constexpr int J = S::J;
+    constexpr int KS = D / 16;
+    constexpr int NT = D / 8;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * S::kStage);
+    int32_t* prefix = reinterpret_cast<int32_t*>(bars + 2 * STAGES);  // [nseg + 1]
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int nseg = static_cast<int>(p.nseg);
+    const uint32_t cap_tokens = p.pitch * 16u;
+
+    // 1. stage counts of every segment, then an inclusive scan (warp 0).
+    for (int sg = tid; sg < nseg; sg += kFastThreads) {
+        const int c = p.ctx[sg / p.head_groups];
+        const bool ok = c > 0 && static_cast<uint32_t>(c) <= cap_tokens;
+        if (!ok && blockIdx.x == 0 && sg % p.head_groups == 0) record_error(p.err, kErrBadContext);
+        const uint32_t units = ok ? (static_cast<uint32_t>(c) + 15u) / 16u : 0u;
+        prefix[sg + 1] = static_cast<int32_t>((units + J - 1) / J);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        int32_t running = 0;
+        for (int base = 0; base < nseg; base += 32) {
+            const int i = base + lane;
+            int32_t v = i < nseg ? prefix[i + 1] : 0;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int32_t t = __shfl_up_sync(0xffffffffu, v, off);
+                if (lane >= off) v += t;
+            }
+            if (i < nseg) prefix[i + 1] = v + running;
+            running += __shfl_sync(0xffffffffu, v, 31);
+        }
+        if (lane == 0) prefix[0] = 0;
+    }
+    __syncthreads();
+    const uint32_t total = static_cast<uint32_t>(prefix[nseg]);
+    if (blockIdx.x == 0)
+        for (int i = tid; i <= nseg; i += kFastThreads) p.seg_prefix[i] = prefix[i];
+    // The combine may be scheduled from here on; it waits (griddepcontrol.wait)
+    // for this whole grid before it reads anything.
+    grid_launch_dependents();
+    const uint32_t x0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * total / gridDim.x);
+    const uint32_t x1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * total / gridDim.x);
+    if (x0 >= x1) return;
+    const int sg0 = find_segment(prefix, nseg, x0);
+
+    const uint32_t full0 = smem_u32(bars);
+    const uint32_t empty0 = smem_u32(bars + STAGES);
+    if (tid == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, kFastComputeWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kFastComputeWarps) {
+        // Producer warp: lane 0 issues; all lanes keep a 32-entry window of
+        // the current segment's block table so entries arrive 32 at a time.
+        const uint64_t policy = l2_policy_evict_first();
+        if (lane == 0) prefetch_tensormap(&tmap);
+        int sg = sg0;
+        uint32_t seg_begin = prefix[sg], seg_end = prefix[sg + 1];
+        int seq = sg / p.head_groups, hg = sg % p.head_groups;
+        uint32_t units = (static_cast<uint32_t>(p.ctx[seq]) + 15u) / 16u;
+        const int32_t* row = p.tables + static_cast<size_t>(seq) * p.pitch;
+        int win = -1;
+        int32_t entry = 0;
+        for (uint32_t x = x0; x < x1; ++x) {
+            if (x >= seg_end) {
+                do {
+                    ++sg;
+                    seg_begin = prefix[sg];
+                    seg_end = prefix[sg + 1];
+                } while (x >= seg_end);
+                seq = sg / p.head_groups;
+                hg = sg % p.head_groups;
+                units = (static_cast<uint32_t>(p.ctx[seq]) + 15u) / 16u;
+                row = p.tables + static_cast<size_t>(seq) * p.pitch;
+                win = -1;
+            }
+            const uint32_t it = x - x0;
+            const uint32_t slot = it % STAGES;
+            const int blk0 = static_cast<int>((x - seg_begin) * J);
+            if (win < 0 || blk0 + J > win + 32) {
+                win = blk0;
+                entry = (static_cast<uint32_t>(win + lane) < units) ? row[win + lane] : 0;
+            }
+            int32_t ids[J];
+#pragma unroll
+            for (int j = 0; j < J; ++j) ids[j] = __shfl_sync(0xffffffffu, entry, blk0 - win + j);
+            int ok = 1;
+            if (lane == 0) {
+                if (it >= STAGES && !mbar_wait_bounded(empty0 + 8 * slot, ((it / STAGES) - 1) & 1u)) {
+                    record_error(p.err, kErrWaitTimeout);
+                    ok = 0;
+                } else {
+                    const uint32_t nb = min(static_cast<uint32_t>(J), units - static_cast<uint32_t>(blk0));
+                    mbar_arrive_expect_tx(full0 + 8 * slot, nb * S::kBlock);
+                    const uint32_t dst = smem_u32(smem + slot * S::kStage);
+#pragma unroll
+                    for (int j = 0; j < J; ++j) {
+                        if (static_cast<uint32_t>(j) < nb) {
+                            int32_t id = ids[j];
+                            if (static_cast<uint32_t>(id) >= p.num_blocks) {
+                                record_error(p.err, kErrBadBlockId);
+                                id = 0;
+                            }
+                            const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
+                            tma_load_4d(dst + j * S::kBlock, &tmap, full0 + 8 * slot, 0, r, hg * HH, 0, policy);
+                            tma_load_4d(dst + j * S::kBlock + S::kBox, &tmap, full0 + 8 * slot, 0, r + 16,
+                                        hg * HH, 0, policy);
+                        }
+                    }
+                }
+            }
+            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
+        }
+        return;
+    }
+
+    // Consumer warps: (hh, j) owns kv head hg*HH + hh and unit j of each stage.
+    const int hh = warp % HH;
+    const int j = warp / HH;
+    const int g = lane >> 2;
+    const int c = lane & 3;
+    const int G = static_cast<int>(p.group);
+
+    int sg = sg0;
+    uint32_t seg_begin = prefix[sg], seg_end = prefix[sg + 1];
+    int seq = sg / p.head_groups, hg = sg % p.head_groups;
+    int ctx = p.ctx[seq];
+    uint32_t units = (static_cast<uint32_t>(ctx) + 15u) / 16u;
+
+    uint32_t qa[KS][4];
+    WarpState<D> st;
+
+    // Writes this warp's partial (accumulator rows < G, max, sum) for the
+    // current segment piece as record (sg + blockIdx.x, hh, j).
+    auto flush = [&]() {
+        float a0 = st.l0 + __shfl_xor_sync(0xffffffffu, st.l0, 1);
+        a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
+        float a1 = st.l1 + __shfl_xor_sync(0xffffffffu, st.l1, 1);
+        a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
+        const size_t rec = ((static_cast<size_t>(sg) + blockIdx.x) * HH + hh) * J + j;
+        float* wo = p.rec_acc + rec * G * D;
+#pragma unroll
+        for (int n = 0; n < NT; ++n) {
+            const int col = n * 8 + c * 2;
+            if (g < G) *reinterpret_cast<float2*>(wo + g * D + col) = make_float2(st.o[n][0], st.o[n][1]);
+            if (g + 8 < G) *reinterpret_cast<float2*>(wo + (g + 8) * D + col) = make_float2(st.o[n][2], st.o[n][3]);
+        }
+        if (c == 0) {
+            if (g < G) p.rec_ml[rec * G + g] = make_float2(st.m0, a0);
+            if (g + 8 < G) p.rec_ml[rec * G + g + 8] = make_float2(st.m1, a1);
+        }
+    };
+
+    load_query_fragments<D>(qa, p.q, seq, p.hq, hg * HH + hh, G, lane);
+    st.reset();
+    for (uint32_t x = x0; x < x1; ++x) {
+        if (x >= seg_end) {
+            flush();
+            do {
+                ++sg;
+                seg_begin = prefix[sg];
+                seg_end = prefix[sg + 1];
+            } while (x >= seg_end);
+            seq = sg / p.head_groups;
+            hg = sg % p.head_groups;
+            ctx = p.ctx[seq];
+            units = (static_cast<uint32_t>(ctx) + 15u) / 16u;
+            load_query_fragments<D>(qa, p.q, seq, p.hq, hg * HH + hh, G, lane);
+            st.reset();
+        }
+        const uint32_t it = x - x0;
+        const uint32_t slot = it % STAGES;
+        if (!mbar_wait_bounded(full0 + 8 * slot, (it / STAGES) & 1u)) {
+            // no barrier follows, so the warp can stop here; the host sees
+            // the error bit and the combine output is not to be trusted
+            record_error(p.err, kErrWaitTimeout);
+            return;
+        }
+        const uint32_t blk = (x - seg_begin) * J + j;
+        if (blk < units) {
+            const int valid = min(16, ctx - static_cast<int>(blk) * 16);
+            const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
+            attend_block<D, HH>(st, qa, kb, kb + S::kBox, hh, valid, p.scale_log2, lane);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * slot);
+    }
+    flush();
+}
+
+// Partials a (segment, kv head) may have for the one-round-trip merge;
+// segments spread over more CTAs take a loop.
+constexpr int kMergeParts = 16;
+constexpr int kCombineThreads = 256;
+
+// Merges the stream-K records of each (segment, kv head) into the output:
+// grid.x = nseg * HH, 256 threads, one float4 of out per thread per pass.
+// Launched as a programmatic dependent of paged_decode_stream; it waits for
+// that grid (griddepcontrol.wait) before reading anything. The (max, sum) of
+// every (row, partial) is fetched in one round trip, turned into normalised
+// weights in shared memory, then each thread issues all its partial loads
+// before summing.
+template <int D, int HH, int J>
+__global__ void __launch_bounds__(kCombineThreads) combine_records(const float* __restrict__ rec_acc,
+                                                                   const float2* __restrict__ rec_ml,
+                                                                   const int32_t* __restrict__ seg_prefix,
+                                                                   __nv_bfloat16* __restrict__ out, uint32_t nseg,
+                                                                   uint32_t head_groups, uint32_t hq, uint32_t group,
+                                                                   uint32_t grid) {
+    __shared__ float2 sml[16][kMergeParts];
+    __shared__ float sw[16][kMergeParts];
+    __shared__ float sinv[16];
+    constexpr int D4 = D / 4;
+    grid_dependency_wait();
+    const uint32_t sg = blockIdx.x / HH;
+    const int hh = blockIdx.x % HH;
+    const int tid = threadIdx.x;
+    const uint32_t ps = static_cast<uint32_t>(seg_prefix[sg]);
+    const uint32_t pe = static_cast<uint32_t>(seg_prefix[sg + 1]);
+    const uint32_t total = static_cast<uint32_t>(seg_prefix[nseg]);
+    if (pe <= ps) return;
+    // CTAs whose stage ranges intersect [ps, pe)
+    const uint32_t cf = static_cast<uint32_t>((static_cast<uint64_t>(ps + 1) * grid - 1) / total);
+    const uint32_t cl = static_cast<uint32_t>((static_cast<uint64_t>(pe) * grid - 1) / total);
+    const int G = static_cast<int>(group);
+    const int nparts = static_cast<int>(cl - cf + 1) * J;
+    const bool may_be_empty = total < grid;
+    const uint32_t seq = sg / head_groups;
+    const uint32_t kvh = (sg % head_groups) * HH + hh;
+    __nv_bfloat16* ob = out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kvh) * G) * D;
+    // record of part k (CTA cf + k / J, warp column k % J)
+    auto rec_of = [&](int k) { return ((static_cast<size_t>(sg) + cf + k / J) * HH + hh) * J + (k % J); };
+    auto part_ml = [&](int k, int r) {
+        if (may_be_empty && cta_is_empty(cf + k / J, total, grid)) return make_float2(-INFINITY, 0.f);
+        return rec_ml[rec_of(k) * G + r];
+    };
+
+    if (nparts <= kMergeParts) {
+        for (int i = tid; i < G * nparts; i += kCombineThreads) sml[i / nparts][i % nparts] = part_ml(i % nparts, i / nparts);
+        __syncthreads();
+        if (tid < G) {
+            float M = -INFINITY;
+            for (int k = 0; k < nparts; ++k) M = fmaxf(M, sml[tid][k].x);
+            float L = 0.f;
+            for (int k = 0; k < kMergeParts; ++k) {
+                const float2 ml = k < nparts ? sml[tid][k] : make_float2(-INFINITY, 0.f);
+                const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+                sw[tid][k] = w;
+                L += w * ml.y;
+            }
+            sinv[tid] = 1.f / L;
+        }
+        __syncthreads();
+        for (int e = tid; e < G * D4; e += kCombineThreads) {
+            const int r = e / D4, d4 = e % D4;
+            float4 v[kMergeParts];
+#pragma unroll
+            for (int k = 0; k < kMergeParts; ++k)
+                if (k < nparts && sw[r][k] != 0.f)
+                    v[k] = reinterpret_cast<const float4*>(rec_acc + (rec_of(k) * G + r) * D)[d4];
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < kMergeParts; ++k) {
+                const float w = k < nparts ? sw[r][k] : 0.f;
+                if (w != 0.f) {
+                    a.x += w * v[k].x;
+                    a.y += w * v[k].y;
+                    a.z += w * v[k].z;
+                    a.w += w * v[k].w;
+                }
+            }
+            const float inv = sinv[r];
+            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4) = pack_bf16x2(a.x * inv, a.y * inv);
+            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
+        }
+    } else {
+        // a long segment spread over many CTAs: per-row loops
+        if (tid < G) {
+            float M = -INFINITY;
+            for (int k = 0; k < nparts; ++k) M = fmaxf(M, part_ml(k, tid).x);
+            float L = 0.f;
+            for (int k = 0; k < nparts; ++k) {
+                const float2 ml = part_ml(k, tid);
+                if (ml.x != -INFINITY) L += exp2f(ml.x - M) * ml.y;
+            }
+            sw[tid][0] = M;
+            sinv[tid] = 1.f / L;
+        }
+        __syncthreads();
+        for (int e = tid; e < G * D4; e += kCombineThreads) {
+            const int r = e / D4, d4 = e % D4;
+            const float M = sw[r][0];
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = 0; k < nparts; ++k) {
+                const float2 ml = part_ml(k, r);
+                if (ml.x == -INFINITY) continue;
+                const float w = exp2f(ml.x - M);
+                const float4 v = reinterpret_cast<const float4*>(rec_acc + (rec_of(k) * G + r) * D)[d4];
+                a.x += w * v.x;
+                a.y += w * v.y;
+                a.z += w * v.z;
+                a.w += w * v.w;
+            }
+            const float inv = sinv[r];
+            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4) = pack_bf16x2(a.x * inv, a.y * inv);
+            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
         }
     }
 }
@@ -619,6 +1036,57 @@ int launch_fast(const qvp_decode_args& a, const DecodePlan& plan, const FastPara
     }
 }
 
+template <int D, int HH, int STAGES>
+int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
+    using S = FastShape<D, HH, STAGES>;
+    constexpr int J = S::J;
+    constexpr uint32_t kMaxSmem = S::kSmem + (kStreamMaxSegments + 1) * 4;
+    static_assert(kMaxSmem <= 232448, "stream decode exceeds the 227 KB shared-memory limit");
+    static bool attr_set = false;
+    auto kern = paged_decode_stream<D, HH, STAGES>;
+    if (!attr_set) {
+        int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
+                            "cudaFuncSetAttribute(stream decode)");
+        if (rc != QVP_OK) return rc;
+        attr_set = true;
+    }
+    CUtensorMap map;
+    int rc = encode_pool_map(a, HH, &map);
+    if (rc != QVP_OK) return rc;
+    const uint32_t smem = S::kSmem + (sp.nseg + 1) * 4;
+    kern<<<plan.grid_ctas, kFastThreads, smem, st>>>(map, sp);
+    rc = check_cuda(cudaGetLastError(), "launch stream decode");
+    if (rc != QVP_OK) return rc;
+
+    // The combine is a programmatic dependent: it may be scheduled while the
+    // decode grid still runs and waits (griddepcontrol.wait) for its results.
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sp.nseg * HH);
+    cfg.blockDim = dim3(kCombineThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, combine_records<D, HH, J>, static_cast<const float*>(sp.rec_acc),
+                                         static_cast<const float2*>(sp.rec_ml),
+                                         static_cast<const int32_t*>(sp.seg_prefix),
+                                         static_cast<__nv_bfloat16*>(a.out), sp.nseg, sp.head_groups, sp.hq,
+                                         sp.group, plan.grid_ctas),
+                      "launch combine_records");
+}
+
+int launch_stream(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
+    const uint32_t D = a.shape.head_dim;
+    switch (plan.heads_per_cta) {
+        case 4: return D == 128 ? launch_stream_t<128, 4, 3>(a, plan, sp, st) : launch_stream_t<64, 4, 6>(a, plan, sp, st);
+        case 2: return D == 128 ? launch_stream_t<128, 2, 3>(a, plan, sp, st) : launch_stream_t<64, 2, 6>(a, plan, sp, st);
+        default: return D == 128 ? launch_stream_t<128, 1, 3>(a, plan, sp, st) : launch_stream_t<64, 1, 6>(a, plan, sp, st);
+    }
+}
+
 }  // namespace
 
 int plan_decode(const qvp_decode_args& a, DecodePlan& plan) {
@@ -659,6 +1127,26 @@ int plan_decode(const qvp_decode_args& a, DecodePlan& plan) {
                 static_cast<uint64_t>(a.num_blocks) * sh.num_layers * 32u < (1ull << 31);
     plan.heads_per_cta = sh.num_kv_heads % 4 == 0 ? 4 : sh.num_kv_heads % 2 == 0 ? 2 : 1;
 
+    if (plan.fast && a.split_tokens == 0) {
+        const uint32_t z = sh.num_kv_heads / plan.heads_per_cta;
+        const uint64_t nseg = static_cast<uint64_t>(a.batch) * z;
+        if (nseg <= static_cast<uint64_t>(kStreamMaxSegments)) {
+            // Persistent stream-K: one CTA per SM over the whole stage stream.
+            plan.stream = true;
+            plan.nseg = static_cast<uint32_t>(nseg);
+            const int sms = device_sm_count();
+            plan.grid_ctas = sms > 0 ? static_cast<uint32_t>(sms) : 148u;
+            const uint32_t J = 8u / plan.heads_per_cta;
+            const size_t records = (static_cast<size_t>(plan.nseg) + plan.grid_ctas) * plan.heads_per_cta * J;
+            plan.records = records;
+            plan.split_tokens = 0;
+            plan.max_splits = 1;
+            plan.workspace_bytes = round_up(records * plan.group * sh.head_dim * sizeof(float), 256) +
+                                   round_up(records * plan.group * sizeof(float2), 256) +
+                                   (static_cast<size_t>(plan.nseg) + 1) * sizeof(int32_t);
+            return QVP_OK;
+        }
+    }
     uint32_t split = a.split_tokens;
     if (split != 0) {
         if (plan.fast && split % 16 != 0)
@@ -704,7 +1192,7 @@ extern "C" int qvp_decode_plan(const qvp_decode_args* args, uint32_t* split_toke
     if (rc != QVP_OK) return rc;
     if (split_tokens) *split_tokens = plan.split_tokens;
     if (num_splits) *num_splits = plan.max_splits;
-    if (fast_path) *fast_path = plan.fast ? 1 : 0;
+    if (fast_path) *fast_path = plan.stream ? 2 : plan.fast ? 1 : 0;
     return QVP_OK;
 }
 
@@ -725,6 +1213,30 @@ extern "C" int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream) {
                                                     round_up(parts * a.shape.head_dim * sizeof(float), 256))
                         : nullptr;
     const uint32_t D = a.shape.head_dim;
+
+    if (plan.stream) {
+        uint8_t* ws = static_cast<uint8_t*>(a.workspace);
+        const size_t acc_bytes = round_up(plan.records * plan.group * D * sizeof(float), 256);
+        const size_t ml_bytes = round_up(plan.records * plan.group * sizeof(float2), 256);
+        StreamParams sp;
+        sp.tables = a.block_tables;
+        sp.ctx = a.context_lens;
+        sp.q = static_cast<const __nv_bfloat16*>(a.query);
+        sp.rec_acc = reinterpret_cast<float*>(ws);
+        sp.rec_ml = reinterpret_cast<float2*>(ws + acc_bytes);
+        sp.seg_prefix = reinterpret_cast<int32_t*>(ws + acc_bytes + ml_bytes);
+        sp.err = a.error_word;
+        sp.pitch = a.max_blocks_per_seq;
+        sp.num_blocks = a.num_blocks;
+        sp.layer = a.layer;
+        sp.num_layers = a.shape.num_layers;
+        sp.hq = a.num_query_heads;
+        sp.group = plan.group;
+        sp.head_groups = a.shape.num_kv_heads / plan.heads_per_cta;
+        sp.nseg = plan.nseg;
+        sp.scale_log2 = a.scale * 1.4426950408889634f;  // log2(e)
+        return launch_stream(a, plan, sp, st);
+    }
 
     if (plan.fast) {
         FastParams fp;

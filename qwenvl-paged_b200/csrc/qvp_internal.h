@@ -24,6 +24,10 @@ inline uint32_t ceil_div(uint32_t a, uint32_t b) { return (a + b - 1) / b; }
 // What one qvp_decode call will launch.
 struct DecodePlan {
     bool fast = false;          // TMA + tensor-core kernel (bf16, D 64/128, 16-token blocks)
+    bool stream = false;        // persistent stream-K form of the fast kernel
+    uint32_t grid_ctas = 0;     // stream: CTAs (one per SM)
+    uint32_t nseg = 0;          // stream: (sequence, head group) segments
+    size_t records = 0;         // stream: partial records in the workspace
     uint32_t group = 0;         // query heads per kv head (G)
     uint32_t heads_per_cta = 0; // kv heads one fast CTA owns (HH)
     uint32_t split_tokens = 0;  // tokens per split-K partition

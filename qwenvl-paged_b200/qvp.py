@@ -193,6 +193,7 @@ def decode_plan(args: DecodeArgs):
     ws = C.c_size_t()
     check(lib.qvp_decode_workspace_size(C.byref(args), C.byref(ws)), "qvp_decode_workspace_size")
     return {"split_tokens": split.value, "num_splits": ns.value, "fast": bool(fast.value),
+            "stream": fast.value == 2,
             "workspace_bytes": ws.value}
 
 

@@ -141,3 +141,35 @@ def test_decode_is_deterministic_across_calls():
     a = gpu_decode(w, pool, q, split_tokens=256)[1]
     b = gpu_decode(w, pool, q, split_tokens=256)[1]
     assert np.array_equal(a, b)
+
+
+# --- persistent stream-K form (the default for split_tokens = 0) -------------
+
+@pytest.mark.parametrize("kw", [
+    dict(batch=300, ctx_lo=1, ctx_hi=40, hq=28, hkv=4, head_dim=128),     # many short segments per CTA
+    dict(batch=1, ctx_lo=20000, ctx_hi=20000, hq=28, hkv=4, head_dim=128),  # one segment over all CTAs
+    dict(batch=3, ctx_lo=1, ctx_hi=5, hq=28, hkv=4, head_dim=128),        # fewer stages than CTAs
+    dict(batch=9, ctx_lo=100, ctx_hi=3000, hq=64, hkv=8, head_dim=128),   # two head groups per sequence
+    dict(batch=7, ctx_lo=1, ctx_hi=2000, hq=16, hkv=2, head_dim=64),
+    dict(batch=5, ctx_lo=50, ctx_hi=900, hq=8, hkv=1, head_dim=128),
+    dict(batch=6, ctx_lo=50, ctx_hi=900, hq=6, hkv=3, head_dim=128),
+])
+def test_stream_k_matches_the_oracle(kw):
+    w = W.small(20 + kw["batch"] + kw["hkv"], dtype="bf16", **kw)
+    out, ref, plan = check(w)
+    assert plan["stream"], plan
+
+
+def test_stream_k_falls_back_to_the_grid_kernel_past_4096_segments():
+    w = W.small(21, batch=4100, ctx_lo=1, ctx_hi=20, hq=28, hkv=4, head_dim=128, dtype="bf16")
+    out, ref, plan = check(w)
+    assert plan["fast"] and not plan["stream"]
+
+
+def test_stream_k_reuses_a_dirty_workspace():
+    # the records need no zero-fill: a second call over garbage matches
+    w = W.small(22, batch=11, ctx_lo=1, ctx_hi=3000, hq=28, hkv=4, head_dim=128, dtype="bf16")
+    pool, q = W.host_inputs(w)
+    a = gpu_decode(w, pool, q)[1]
+    b = gpu_decode(w, pool, q)[1]
+    assert np.array_equal(a, b)
