@@ -159,6 +159,31 @@ QVP_API int qvp_decode_plan(const qvp_decode_args* args, uint32_t* split_tokens,
                     uint32_t* num_splits, int* fast_path);
 QVP_API int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream);
 
+/*
+ * qvp_decode_noalloc: qvp_decode for callers that cannot allocate device
+ * memory. No counterpart in the reference (its CPU kernel needs no scratch).
+ *
+ * Some callers cannot call cudaMalloc: a host process that owns the whole
+ * device-memory budget and gives plugins only the buffers they compute on,
+ * an FFI caller without a device allocator, or a step loop where cudaMalloc
+ * and cudaFree would synchronise the device. This entry point runs the same
+ * kernels as qvp_decode but ignores args->workspace: its scratch is a 16 MiB
+ * array compiled into the library (every GPU that loads the library holds
+ * it until the process exits). The caller still passes pool, tables,
+ * context lengths, queries and output.
+ *   - A batch needing more than 16 MiB of scratch (qvp_decode_workspace_size)
+ *     is refused with QVP_ERR_WORKSPACE before anything is enqueued.
+ *   - It calls no cudaMalloc, cudaFree or other allocating routine. The first
+ *     call on each device looks up the array's device address
+ *     (cudaGetSymbolAddress) with that device current; make that first call
+ *     before any stream capture.
+ *   - Every call shares the one array, which keeps the last call's contents.
+ *     Nothing in it needs to start at zero (the kernels write every scratch
+ *     byte they read), but calls that overlap on the GPU (other streams, other
+ *     threads) race on it: order them on one stream.
+ */
+QVP_API int qvp_decode_noalloc(const qvp_decode_args* args, qvp_stream_t stream);
+
 /* ---------------------------------------------------------------------------
  * Block movers.
  *

@@ -100,6 +100,7 @@ def _load() -> C.CDLL:
         "qvp_decode_workspace_size": (C.c_int, [P(DecodeArgs), P(sz)]),
         "qvp_decode_plan": (C.c_int, [P(DecodeArgs), P(u32), P(u32), P(C.c_int)]),
         "qvp_decode": (C.c_int, [P(DecodeArgs), vp]),
+        "qvp_decode_noalloc": (C.c_int, [P(DecodeArgs), vp]),
         "qvp_copy_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp]),
         "qvp_gather_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
         "qvp_scatter_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
@@ -120,7 +121,7 @@ EXPORTED = [
     "qvp_block_bytes", "qvp_block_stride", "qvp_last_error", "qvp_version", "qvp_device_sm_count",
     "qvp_pool_create", "qvp_pool_destroy", "qvp_pool_base", "qvp_pool_stride", "qvp_pool_num_blocks",
     "qvp_pool_device", "qvp_pool_write", "qvp_pool_read", "qvp_decode_workspace_size",
-    "qvp_decode_plan", "qvp_decode", "qvp_copy_blocks", "qvp_gather_blocks", "qvp_scatter_blocks",
+    "qvp_decode_plan", "qvp_decode", "qvp_decode_noalloc", "qvp_copy_blocks", "qvp_gather_blocks", "qvp_scatter_blocks",
     "qvp_kv_append",
 ]
 
