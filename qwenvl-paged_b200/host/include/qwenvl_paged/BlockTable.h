@@ -1,0 +1,52 @@
+// Per-sequence logical -> physical page table. Same interface and behaviour
+// as the reference (include/qwenvl_paged/BlockTable.h:14-122): entries kept
+// sorted by logical index, lookup misses on a swapped entry, fork clears
+// `writable`. `entries()` order is what a batch step flattens into the device
+// int32 tables.
+#pragma once
+
+#include "qwenvl_paged/Block.h"
+
+#include <cstddef>
+#include <optional>
+#include <vector>
+
+namespace qwenvl_paged {
+
+struct BlockTableEntry {
+    LogicalBlock logical{};
+    PhysicalBlockId physical_id{0};
+    bool writable{true};
+    // Engaged while the block's bytes live in the swap backend; physical_id
+    // is then stale.
+    std::optional<SwapSlotId> swap_slot{};
+};
+
+class BlockTable {
+public:
+    explicit BlockTable(SequenceId sequence_id, CacheKind cache_kind = CacheKind::TextKV);
+
+    [[nodiscard]] SequenceId sequence_id() const noexcept;
+    [[nodiscard]] CacheKind cache_kind() const noexcept;
+    [[nodiscard]] std::size_t size() const noexcept;
+    [[nodiscard]] bool empty() const noexcept;
+
+    void map(LogicalBlock logical, PhysicalBlockId physical_id, bool writable);
+    [[nodiscard]] std::optional<PhysicalBlockId> unmap(LogicalBlockIndex index);
+    [[nodiscard]] std::optional<PhysicalBlockId> lookup(LogicalBlockIndex index) const;
+    [[nodiscard]] const BlockTableEntry* entry(LogicalBlockIndex index) const noexcept;
+    [[nodiscard]] BlockTableEntry* mutable_entry(LogicalBlockIndex index) noexcept;
+    void set_writable(LogicalBlockIndex index, bool writable);
+    [[nodiscard]] const std::vector<BlockTableEntry>& entries() const noexcept;
+    [[nodiscard]] BlockTable fork(SequenceId child_sequence_id) const;
+
+private:
+    // Position of the first entry whose logical index is >= `index`.
+    [[nodiscard]] std::size_t position(LogicalBlockIndex index) const noexcept;
+
+    SequenceId sequence_id_{0};
+    CacheKind cache_kind_{CacheKind::TextKV};
+    std::vector<BlockTableEntry> entries_;
+};
+
+}  // namespace qwenvl_paged

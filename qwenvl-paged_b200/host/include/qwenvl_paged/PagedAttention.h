@@ -1,0 +1,102 @@
+// Paged-decode attention behind the reference's signature.
+//
+// paged_attention_decode<T>(view, query, params, out) keeps the contract of
+// the reference CPU kernel (include/qwenvl_paged/PagedAttention.h:23-127):
+// it returns false and leaves `out` untouched when the arguments do not fit
+// the cache shape or any block of [0, context_len) is unmapped or swapped
+// out. The work runs on the GPU (qvp_decode) on the allocator's stream; T is
+// float or a 2-byte bfloat16 type such as qwenvl_paged::bfloat16, and
+// `query` / `out` may be host or device pointers (host pointers make the call
+// synchronous). PagedDecodeBatch is the batched form an engine step uses.
+#pragma once
+
+#include "qwenvl_paged/CacheLayout.h"
+#include "qwenvl_paged/KVCacheManager.h"
+
+#include <cstddef>
+#include <cstdint>
+#include <cstring>
+#include <string>
+#include <vector>
+
+namespace qwenvl_paged {
+
+struct PagedAttentionParams {
+    std::uint32_t layer{0};
+    std::uint32_t num_query_heads{0};
+    std::uint32_t context_len{0};
+    float scale{1.0F};
+};
+
+// Host bfloat16: exact widening, round-to-nearest-even narrowing.
+struct bfloat16 {
+    std::uint16_t bits{0};
+    bfloat16() = default;
+    explicit bfloat16(float f) noexcept {
+        std::uint32_t u;
+        std::memcpy(&u, &f, 4);
+        if ((u & 0x7fffffffu) > 0x7f800000u)
+            bits = static_cast<std::uint16_t>((u >> 16) | 0x40u);
+        else
+            bits = static_cast<std::uint16_t>((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+    }
+    explicit operator float() const noexcept {
+        const std::uint32_t u = static_cast<std::uint32_t>(bits) << 16;
+        float f;
+        std::memcpy(&f, &u, 4);
+        return f;
+    }
+};
+static_assert(sizeof(bfloat16) == 2, "bfloat16 is two bytes");
+
+namespace detail {
+// Type-erased body of paged_attention_decode<T>; elem_bytes = sizeof(T).
+bool decode_one(const CacheView& view, const void* query, std::size_t elem_bytes,
+                const PagedAttentionParams& params, void* out);
+}  // namespace detail
+
+template <typename T>
+[[nodiscard]] bool paged_attention_decode(const CacheView& view, const T* query, const PagedAttentionParams& params,
+                                          T* out) {
+    return detail::decode_one(view, query, sizeof(T), params, out);
+}
+
+// Batched decode of one layer for an engine step. Each call validates every
+// view on the host (any failure: false, nothing enqueued, `out` untouched),
+// flattens the block tables into a pinned int32 [batch][max_blocks] buffer,
+// uploads it and the context lengths with one cudaMemcpyAsync each, and
+// launches qvp_decode on the allocator's stream. `query` and `out` are device
+// arrays [batch][num_query_heads][head_dim] in the pool's element type.
+// Buffers are kept and reused across calls.
+class PagedDecodeBatch {
+public:
+    explicit PagedDecodeBatch(const MemoryAllocator& allocator);
+    ~PagedDecodeBatch();
+    PagedDecodeBatch(const PagedDecodeBatch&) = delete;
+    PagedDecodeBatch& operator=(const PagedDecodeBatch&) = delete;
+
+    bool run(const std::vector<CacheView>& views, const std::vector<std::uint32_t>& context_lens,
+             std::uint32_t layer, std::uint32_t num_query_heads, float scale, const void* query, void* out);
+
+    // qvp_status of the last run (0 = OK) and its text.
+    [[nodiscard]] int last_status() const noexcept { return status_; }
+    [[nodiscard]] const std::string& last_error() const noexcept { return error_; }
+    // Device error bits (qvp_decode error_word) of the last run; waits for it.
+    [[nodiscard]] int device_error();
+
+private:
+    bool grow(std::size_t table_ints, std::size_t batch, std::size_t workspace);
+
+    const MemoryAllocator* allocator_;
+    std::int32_t* host_buf_{nullptr};    // pinned: tables then context lengths
+    std::int32_t* dev_buf_{nullptr};
+    std::size_t buf_ints_{0};
+    void* workspace_{nullptr};
+    std::size_t workspace_bytes_{0};
+    std::int32_t* error_word_{nullptr};
+    void* upload_event_{nullptr};
+    int status_{0};
+    std::string error_;
+};
+
+}  // namespace qwenvl_paged

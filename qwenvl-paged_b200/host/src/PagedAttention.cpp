@@ -1,0 +1,290 @@
+#include "qwenvl_paged/PagedAttention.h"
+
+#include "qvp.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+namespace qwenvl_paged {
+
+namespace {
+
+struct OnDevice {
+    int prev = -1;
+    bool switched = false;
+    explicit OnDevice(int device) {
+        if (device >= 0 && cudaGetDevice(&prev) == cudaSuccess && prev != device &&
+            cudaSetDevice(device) == cudaSuccess)
+            switched = true;
+        cudaGetLastError();
+    }
+    ~OnDevice() {
+        if (switched) cudaSetDevice(prev);
+    }
+};
+
+bool is_device_pointer(const void* p) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+// The host-side checks of the reference kernel (PagedAttention.h:59-89):
+// shape/argument consistency, then every block of [0, context_len) must be
+// resolvable. Appends the physical ids of those blocks to `ids`.
+bool resolve(const CacheView& view, std::size_t elem_bytes, std::uint32_t layer, std::uint32_t num_query_heads,
+             std::uint32_t context_len, std::vector<std::int32_t>& ids) {
+    if (!view.valid()) return false;
+    const BlockShape& sh = view.layout.shape;
+    if (elem_bytes != sh.bytes_per_element || context_len == 0 || layer >= sh.num_layers ||
+        num_query_heads == 0 || num_query_heads % sh.num_kv_heads != 0)
+        return false;
+    const std::uint32_t tpb = sh.tokens_per_block;
+    const std::uint32_t nblk = (context_len + tpb - 1) / tpb;
+    for (std::uint32_t i = 0; i < nblk; ++i) {
+        const std::optional<PhysicalBlockId> id = view.block_table->lookup(i);
+        if (!id || view.allocator->block(*id) == nullptr) return false;
+        ids.push_back(static_cast<std::int32_t>(*id));
+    }
+    return true;
+}
+
+int dtype_for(std::size_t elem_bytes) {
+    return elem_bytes == 4 ? QVP_DTYPE_F32 : elem_bytes == 2 ? QVP_DTYPE_BF16 : -1;
+}
+
+qvp_decode_args base_args(const MemoryAllocator& alloc, std::size_t elem_bytes, std::uint32_t layer,
+                          std::uint32_t num_query_heads, float scale) {
+    qvp_decode_args a{};
+    const BlockShape& sh = alloc.block_shape();
+    a.pool = alloc.pool_base();
+    a.block_stride = alloc.block_stride();
+    a.num_blocks = alloc.num_blocks();
+    a.shape = {sh.tokens_per_block, sh.num_layers, sh.num_kv_heads, sh.head_dim, sh.bytes_per_element};
+    a.dtype = dtype_for(elem_bytes);
+    a.layer = layer;
+    a.num_query_heads = num_query_heads;
+    a.scale = scale;
+    return a;
+}
+
+// Device scratch of the single-sequence shim, grown on demand.
+struct ShimBuffers {
+    int device = -1;
+    void* mem = nullptr;
+    std::size_t bytes = 0;
+    ~ShimBuffers() {
+        if (mem != nullptr) cudaFree(mem);
+    }
+    std::byte* get(std::size_t need, int dev) {
+        if (mem != nullptr && (need > bytes || dev != device)) {
+            cudaFree(mem);
+            mem = nullptr;
+            bytes = 0;
+        }
+        if (mem == nullptr) {
+            const std::size_t n = std::max<std::size_t>(need, 1 << 20);
+            if (cudaMalloc(&mem, n) != cudaSuccess) {
+                cudaGetLastError();
+                return nullptr;
+            }
+            bytes = n;
+            device = dev;
+        }
+        return static_cast<std::byte*>(mem);
+    }
+};
+
+std::size_t align256(std::size_t v) { return (v + 255) / 256 * 256; }
+
+}  // namespace
+
+namespace detail {
+
+bool decode_one(const CacheView& view, const void* query, std::size_t elem_bytes, const PagedAttentionParams& params,
+                void* out) {
+    if (query == nullptr || out == nullptr) return false;
+    std::vector<std::int32_t> ids;
+    if (!resolve(view, elem_bytes, params.layer, params.num_query_heads, params.context_len, ids)) return false;
+    MemoryAllocator& alloc = const_cast<MemoryAllocator&>(*view.allocator);
+    if (!alloc.has_storage() || dtype_for(elem_bytes) < 0) return false;
+    OnDevice guard(alloc.device());
+    alloc.flush();  // queued copy-on-write copies land before the decode reads
+
+    const BlockShape& sh = view.layout.shape;
+    const std::size_t qo_bytes = static_cast<std::size_t>(params.num_query_heads) * sh.head_dim * elem_bytes;
+    qvp_decode_args a = base_args(alloc, elem_bytes, params.layer, params.num_query_heads, params.scale);
+    a.batch = 1;
+    a.max_blocks_per_seq = static_cast<std::uint32_t>(ids.size());
+    a.max_context_len = params.context_len;
+    a.block_tables = reinterpret_cast<const std::int32_t*>(0x10);  // placeholders for the size query
+    a.context_lens = reinterpret_cast<const std::int32_t*>(0x10);
+    a.query = query;
+    a.out = out;
+    std::size_t ws = 0;
+    if (qvp_decode_workspace_size(&a, &ws) != QVP_OK) return false;
+
+    const bool q_dev = is_device_pointer(query);
+    const bool o_dev = is_device_pointer(out);
+    const std::size_t tab_off = 0;
+    const std::size_t q_off = align256(tab_off + (ids.size() + 1) * sizeof(std::int32_t));
+    const std::size_t o_off = align256(q_off + qo_bytes);
+    const std::size_t ws_off = align256(o_off + qo_bytes);
+    static thread_local ShimBuffers buffers;
+    std::byte* base = buffers.get(ws_off + ws, alloc.device());
+    if (base == nullptr) return false;
+
+    cudaStream_t st = alloc.stream();
+    ids.push_back(static_cast<std::int32_t>(params.context_len));  // the context length follows the table row
+    cudaMemcpyAsync(base + tab_off, ids.data(), ids.size() * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
+    a.block_tables = reinterpret_cast<const std::int32_t*>(base + tab_off);
+    a.context_lens = reinterpret_cast<const std::int32_t*>(base + tab_off) + (ids.size() - 1);
+    if (!q_dev) {
+        cudaMemcpyAsync(base + q_off, query, qo_bytes, cudaMemcpyHostToDevice, st);
+        a.query = base + q_off;
+    }
+    a.out = o_dev ? out : static_cast<void*>(base + o_off);
+    a.workspace = ws ? base + ws_off : nullptr;
+    a.workspace_bytes = ws;
+    if (qvp_decode(&a, st) != QVP_OK) return false;
+    // One sequence per call: wait for it, so the caller's host buffers are
+    // free to reuse on return. A host `out` is written only after success.
+    if (cudaStreamSynchronize(st) != cudaSuccess) return false;
+    if (!o_dev && cudaMemcpy(out, base + o_off, qo_bytes, cudaMemcpyDeviceToHost) != cudaSuccess) return false;
+    return true;
+}
+
+}  // namespace detail
+
+PagedDecodeBatch::PagedDecodeBatch(const MemoryAllocator& allocator) : allocator_(&allocator) {}
+
+PagedDecodeBatch::~PagedDecodeBatch() {
+    OnDevice guard(allocator_->device());
+    cudaStreamSynchronize(allocator_->stream());
+    if (host_buf_ != nullptr) cudaFreeHost(host_buf_);
+    if (dev_buf_ != nullptr) cudaFree(dev_buf_);
+    if (workspace_ != nullptr) cudaFree(workspace_);
+    if (error_word_ != nullptr) cudaFree(error_word_);
+    if (upload_event_ != nullptr) cudaEventDestroy(static_cast<cudaEvent_t>(upload_event_));
+}
+
+bool PagedDecodeBatch::grow(std::size_t ints, std::size_t /*batch*/, std::size_t workspace) {
+    if (upload_event_ == nullptr) {
+        cudaEvent_t ev;
+        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) return false;
+        upload_event_ = ev;
+    }
+    if (error_word_ == nullptr) {
+        if (cudaMalloc(reinterpret_cast<void**>(&error_word_), sizeof(std::int32_t)) != cudaSuccess) return false;
+        cudaMemset(error_word_, 0, sizeof(std::int32_t));
+    }
+    if (ints > buf_ints_) {
+        cudaStreamSynchronize(allocator_->stream());
+        if (host_buf_ != nullptr) cudaFreeHost(host_buf_);
+        if (dev_buf_ != nullptr) cudaFree(dev_buf_);
+        host_buf_ = nullptr;
+        dev_buf_ = nullptr;
+        buf_ints_ = 0;
+        const std::size_t n = std::max<std::size_t>(ints * 2, 4096);
+        if (cudaMallocHost(reinterpret_cast<void**>(&host_buf_), n * sizeof(std::int32_t)) != cudaSuccess ||
+            cudaMalloc(reinterpret_cast<void**>(&dev_buf_), n * sizeof(std::int32_t)) != cudaSuccess)
+            return false;
+        buf_ints_ = n;
+    }
+    if (workspace > workspace_bytes_) {
+        cudaStreamSynchronize(allocator_->stream());
+        if (workspace_ != nullptr) cudaFree(workspace_);
+        workspace_ = nullptr;
+        workspace_bytes_ = 0;
+        if (cudaMalloc(&workspace_, workspace) != cudaSuccess) return false;
+        workspace_bytes_ = workspace;
+    }
+    return true;
+}
+
+bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vector<std::uint32_t>& context_lens,
+                           std::uint32_t layer, std::uint32_t num_query_heads, float scale, const void* query,
+                           void* out) {
+    status_ = QVP_ERR_INVALID;
+    error_.clear();
+    if (views.size() != context_lens.size() || query == nullptr || out == nullptr) {
+        error_ = "views and context lengths differ in count, or a null buffer";
+        return false;
+    }
+    const std::size_t B = views.size();
+    if (B == 0) {
+        status_ = QVP_OK;
+        return true;
+    }
+    const std::size_t elem = allocator_->block_shape().bytes_per_element;
+    std::vector<std::vector<std::int32_t>> rows(B);
+    std::uint32_t pitch = 1, max_ctx = 1;
+    for (std::size_t b = 0; b < B; ++b) {
+        if (views[b].allocator != allocator_ ||
+            !resolve(views[b], elem, layer, num_query_heads, context_lens[b], rows[b])) {
+            error_ = "sequence " + std::to_string(b) + " cannot be read (argument mismatch, or an unmapped or "
+                     "swapped-out block inside its context)";
+            status_ = QVP_ERR_UNMAPPED;
+            return false;
+        }
+        pitch = std::max<std::uint32_t>(pitch, static_cast<std::uint32_t>(rows[b].size()));
+        max_ctx = std::max(max_ctx, context_lens[b]);
+    }
+    MemoryAllocator& alloc = const_cast<MemoryAllocator&>(*allocator_);
+    OnDevice guard(alloc.device());
+    alloc.flush();
+    qvp_decode_args a = base_args(alloc, elem, layer, num_query_heads, scale);
+    a.batch = static_cast<std::uint32_t>(B);
+    a.max_blocks_per_seq = pitch;
+    a.max_context_len = max_ctx;
+    a.block_tables = reinterpret_cast<const std::int32_t*>(0x10);
+    a.context_lens = reinterpret_cast<const std::int32_t*>(0x10);
+    a.query = query;
+    a.out = out;
+    std::size_t ws = 0;
+    status_ = qvp_decode_workspace_size(&a, &ws);
+    if (status_ != QVP_OK) {
+        error_ = qvp_last_error();
+        return false;
+    }
+    const std::size_t ints = B * pitch + B;
+    if (!grow(ints, B, ws)) {
+        status_ = QVP_ERR_NOMEM;
+        error_ = "could not allocate decode buffers";
+        return false;
+    }
+    // the previous step's upload must have left the pinned buffer
+    cudaEventSynchronize(static_cast<cudaEvent_t>(upload_event_));
+    for (std::size_t b = 0; b < B; ++b) {
+        std::int32_t* row = host_buf_ + b * pitch;
+        std::copy(rows[b].begin(), rows[b].end(), row);
+        std::fill(row + rows[b].size(), row + pitch, -1);
+        host_buf_[B * pitch + b] = static_cast<std::int32_t>(context_lens[b]);
+    }
+    cudaStream_t st = alloc.stream();
+    cudaMemcpyAsync(dev_buf_, host_buf_, ints * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
+    cudaEventRecord(static_cast<cudaEvent_t>(upload_event_), st);
+    a.block_tables = dev_buf_;
+    a.context_lens = dev_buf_ + B * pitch;
+    a.workspace = ws ? workspace_ : nullptr;
+    a.workspace_bytes = ws ? workspace_bytes_ : 0;
+    a.error_word = error_word_;
+    status_ = qvp_decode(&a, st);
+    if (status_ != QVP_OK) error_ = qvp_last_error();
+    return status_ == QVP_OK;
+}
+
+int PagedDecodeBatch::device_error() {
+    if (error_word_ == nullptr) return 0;
+    OnDevice guard(allocator_->device());
+    std::int32_t v = 0;
+    cudaStreamSynchronize(allocator_->stream());
+    cudaMemcpy(&v, error_word_, sizeof(v), cudaMemcpyDeviceToHost);
+    return v;
+}
+
+}  // namespace qwenvl_paged
