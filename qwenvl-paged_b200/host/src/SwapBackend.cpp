@@ -103,7 +103,11 @@ const std::byte* DeviceSwapBackend::slot_bytes(SwapSlotId slot) const noexcept {
 }
 
 std::optional<SwapSlotId> DeviceSwapBackend::store(const PhysicalBlock& block) {
-    if (!ready() || slots_.size() >= max_slots_ || free_indices_.empty()) return std::nullopt;
+    if (!ready() || slots_.size() >= max_slots_) return std::nullopt;
+    // capacity counts resident slots, as in the reference; slab slots freed
+    // by a discard while moves were queued become usable after a flush
+    if (free_indices_.empty() && !release_after_flush_.empty()) flush();
+    if (free_indices_.empty()) return std::nullopt;
     if (block.data() != allocator_->pool_base() + static_cast<std::size_t>(block.id()) * allocator_->block_stride())
         return std::nullopt;  // not a block of this backend's pool
     if (!pending_loads_.empty()) flush_loads();
