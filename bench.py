@@ -167,14 +167,22 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     launches_per_step = 2 if plan["stream"] else 1 + (1 if plan["num_splits"] > 1 else 0)
+    # (the NCCL all-gather of cfg4 shards is a library collective, not counted)
     kernel_name = ("paged_decode_stream (persistent stream-K, TMA + mma.sync) + combine_records" if plan["stream"]
                    else "paged_decode_fast (grid split-K, TMA + mma.sync) + combine_partitions" if plan["fast"]
                    else "paged_decode_generic + combine_partitions")
+
+    gather = scaling == "strong" and world > 1 and not args.no_gather
+    if gather:
+        import sharding
 
     def step():
         st = qvp.decode(a, sh)
         if st != 0:
             raise RuntimeError(f"qvp_decode failed: {st} {qvp.last_error()}")
+        if gather:
+            # a consumer that needs every head: all-gather [B, Hq/N, D] (NCCL)
+            sharding.all_gather_heads(out)
 
     def barrier():
         if world > 1:
@@ -218,7 +226,8 @@ def run_ours(args):
 
     ms_step = total_ms / args.steps
     alg = w.algorithmic_bytes()
-    world_bytes = alg * (world if scaling == "weak" else 1)
+    # every rank moves its own algorithmic bytes (its batch, or its heads)
+    world_bytes = alg * world
     value = world_bytes / (ms_step * 1e-3) / 1e9
     peak, peak_kind = measured_peak()
     achieved = alg / (ms_step * 1e-3) / 1e9  # per GPU
@@ -282,7 +291,8 @@ def run_ours(args):
                 "num_splits_max": plan["num_splits"],
                 "kernel": kernel_name,
                 "l2": f"inputs larger than L2 ({w.kv_bytes() / 1e6:.0f} MB of K/V read per step)",
-                "parallelism": f"dp{world}" if scaling == "weak" else f"kv-head shards x{world}",
+                "parallelism": f"dp{world}" if scaling == "weak" else
+                f"kv-head shards x{world}" + (" + NCCL all-gather of outputs" if world > 1 and not args.no_gather else ""),
             },
             "seqs_per_s": round(w.batch * (world if scaling == "weak" else 1) / (ms_step * 1e-3), 1),
             "roofline": {
@@ -434,6 +444,7 @@ def main():
     p.add_argument("--split", type=int, default=0, help="split-K partition in tokens (0 = auto)")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    p.add_argument("--no-gather", action="store_true", help="cfg4 shards: skip the output all-gather")
     p.add_argument("--profile", action="store_true",
                    help="for ncu: only warm-up and timed decode steps (no clock probe, e2e or CPU baseline)")
     args = p.parse_args()
