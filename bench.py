@@ -42,10 +42,10 @@ import workloads as W  # noqa: E402
 METRIC = "paged-decode KV GB/s (% of HBM peak) and seqs/s at 1/2/4/8 B200 vs host CPU"
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one decode step of the
-# default workload, from the ncu capture summarised in
-# profiles/paged_decode_fast_cfg2.md (None until captured).
-NCU_TRAFFIC_BYTES = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
+# kernel (paged_decode_stream) on the default workload, from the ncu capture
+# summarised in profiles/paged_decode_stream_cfg2.md.
+NCU_TRAFFIC_BYTES = {"cfg2-qwen2vl-7b-decode": 603_610_368 + 5_478_912}
 
 
 def measured_peak():
