@@ -434,13 +434,37 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_scenario(args):
+    """cfg3 / cfg5 through the C++ host layer (qwenvl-paged_b200/scenarios),
+    one JSON line with the scenario's own measurements."""
+    import ctypes as C
+    lib = C.CDLL(os.path.join(ROOT, "qwenvl-paged_b200", "lib", "libqvp_scenarios.so"))
+    buf = C.create_string_buffer(1 << 16)
+    if args.workload == "cfg3":
+        lib.qvp_scenario_cow.argtypes = [C.c_int] * 6 + [C.c_char_p, C.c_size_t]
+        rc = lib.qvp_scenario_cow(16, 8, 2048, 64, 3, max(args.steps, 1), buf, len(buf))
+        metric, key, unit = "copy-on-write materialisation, batched copy kernel GB/s (read+write)", "cow_gbs", "GB/s"
+    else:
+        lib.qvp_scenario_swap.argtypes = [C.c_uint32, C.c_double, C.c_double, C.c_int, C.c_int, C.c_char_p,
+                                          C.c_size_t]
+        rc = lib.qvp_scenario_swap(args.swap_pool_blocks, 0.9, 0.25, 64, 5, buf, len(buf))
+        metric, key, unit = "swap-out GB/s to pinned host memory (gather kernel + cudaMemcpyAsync)", "swap_out_gbs", "GB/s"
+    if rc < 0:
+        raise SystemExit("scenario output overflow")
+    d = json.loads(buf.value.decode())
+    line = {"metric": metric, "value": d.get(key), "unit": unit, "n_gpus": 1, "higher_is_better": True,
+            "data": "synthetic: seeded context lengths, branch lengths and preemption choices", "config": d}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["cfg2", "cfg1", "cfg4"], default="cfg2")
+    p.add_argument("--workload", choices=["cfg2", "cfg1", "cfg4", "cfg3", "cfg5"], default="cfg2")
+    p.add_argument("--swap-pool-blocks", type=int, default=1 << 20, help="cfg5 pool size in 64 KiB blocks")
     p.add_argument("--split", type=int, default=0, help="split-K partition in tokens (0 = auto)")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
@@ -450,7 +474,9 @@ def main():
     args = p.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload in ("cfg3", "cfg5") and args.impl == "ours":
+        run_scenario(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

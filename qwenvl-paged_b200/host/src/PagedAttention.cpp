@@ -53,6 +53,31 @@ bool resolve(const CacheView& view, std::size_t elem_bytes, std::uint32_t layer,
     return true;
 }
 
+// The arguments part of resolve(), without walking the table.
+bool arguments_fit(const CacheView& view, std::size_t elem_bytes, std::uint32_t layer, std::uint32_t num_query_heads,
+                   std::uint32_t context_len) {
+    if (!view.valid()) return false;
+    const BlockShape& sh = view.layout.shape;
+    return elem_bytes == sh.bytes_per_element && context_len != 0 && layer < sh.num_layers && num_query_heads != 0 &&
+           num_query_heads % sh.num_kv_heads == 0;
+}
+
+// Writes the physical ids of blocks [0, nblk) into `row` by one pass over the
+// table's sorted entries; false if any of them is unmapped or swapped (the
+// same blocks resolve() would refuse).
+bool write_row(const CacheView& view, std::uint32_t nblk, std::int32_t* row) {
+    const std::vector<BlockTableEntry>& es = view.block_table->entries();
+    const std::uint32_t limit = view.allocator->num_blocks();
+    if (es.size() < nblk) return false;
+    for (std::uint32_t i = 0; i < nblk; ++i) {
+        const BlockTableEntry& e = es[i];
+        // sorted and unique: entry i maps logical block i iff its index is i
+        if (e.logical.index != i || e.swap_slot.has_value() || e.physical_id >= limit) return false;
+        row[i] = static_cast<std::int32_t>(e.physical_id);
+    }
+    return true;
+}
+
 int dtype_for(std::size_t elem_bytes) {
     return elem_bytes == 4 ? QVP_DTYPE_F32 : elem_bytes == 2 ? QVP_DTYPE_BF16 : -1;
 }
@@ -221,22 +246,19 @@ bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vecto
         return true;
     }
     const std::size_t elem = allocator_->block_shape().bytes_per_element;
-    std::vector<std::vector<std::int32_t>> rows(B);
+    const std::uint32_t tpb = allocator_->block_shape().tokens_per_block;
     std::uint32_t pitch = 1, max_ctx = 1;
     for (std::size_t b = 0; b < B; ++b) {
         if (views[b].allocator != allocator_ ||
-            !resolve(views[b], elem, layer, num_query_heads, context_lens[b], rows[b])) {
-            error_ = "sequence " + std::to_string(b) + " cannot be read (argument mismatch, or an unmapped or "
-                     "swapped-out block inside its context)";
-            status_ = QVP_ERR_UNMAPPED;
+            !arguments_fit(views[b], elem, layer, num_query_heads, context_lens[b])) {
+            error_ = "sequence " + std::to_string(b) + " does not fit the cache shape";
             return false;
         }
-        pitch = std::max<std::uint32_t>(pitch, static_cast<std::uint32_t>(rows[b].size()));
+        pitch = std::max<std::uint32_t>(pitch, (context_lens[b] + tpb - 1) / tpb);
         max_ctx = std::max(max_ctx, context_lens[b]);
     }
     MemoryAllocator& alloc = const_cast<MemoryAllocator&>(*allocator_);
     OnDevice guard(alloc.device());
-    alloc.flush();
     qvp_decode_args a = base_args(alloc, elem, layer, num_query_heads, scale);
     a.batch = static_cast<std::uint32_t>(B);
     a.max_blocks_per_seq = pitch;
@@ -261,10 +283,17 @@ bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vecto
     cudaEventSynchronize(static_cast<cudaEvent_t>(upload_event_));
     for (std::size_t b = 0; b < B; ++b) {
         std::int32_t* row = host_buf_ + b * pitch;
-        std::copy(rows[b].begin(), rows[b].end(), row);
-        std::fill(row + rows[b].size(), row + pitch, -1);
+        const std::uint32_t nblk = (context_lens[b] + tpb - 1) / tpb;
+        if (!write_row(views[b], nblk, row)) {
+            status_ = QVP_ERR_UNMAPPED;
+            error_ = "sequence " + std::to_string(b) +
+                     " has an unmapped or swapped-out block inside its context";
+            return false;
+        }
+        std::fill(row + nblk, row + pitch, -1);
         host_buf_[B * pitch + b] = static_cast<std::int32_t>(context_lens[b]);
     }
+    alloc.flush();  // queued copy-on-write copies and swap moves land first
     cudaStream_t st = alloc.stream();
     cudaMemcpyAsync(dev_buf_, host_buf_, ints * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
     cudaEventRecord(static_cast<cudaEvent_t>(upload_event_), st);

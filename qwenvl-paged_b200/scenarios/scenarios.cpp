@@ -1,0 +1,343 @@
+// Benchmark scenarios that exercise the host layer end to end on one GPU:
+//   cfg3  copy-on-write parallel sampling (fork a prompt into n branches, let
+//         every branch append private tokens, materialise the shared last
+//         block with one batched copy launch, decode all branches);
+//   cfg5  preemption / swap churn on a 1,048,576-block pool (swap out a
+//         seeded quarter of the resident sequences to pinned host memory,
+//         decode the rest, swap them back in).
+// Each returns one JSON object of measurements. Loaded by bench.py
+// (--workload cfg3 / cfg5) from qwenvl-paged_b200/lib/libqvp_scenarios.so.
+#include "qwenvl_paged/KVCacheManager.h"
+#include "qwenvl_paged/MemoryAllocator.h"
+#include "qwenvl_paged/PagedAttention.h"
+#include "qwenvl_paged/SwapBackend.h"
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <sstream>
+#include <string>
+#include <vector>
+
+using namespace qwenvl_paged;
+
+namespace {
+
+BlockShape bf16_shape(std::uint32_t heads) {
+    BlockShape s;
+    s.tokens_per_block = 16;
+    s.num_layers = 1;
+    s.num_kv_heads = heads;
+    s.head_dim = 128;
+    s.bytes_per_element = 2;
+    return s;
+}
+
+struct Events {
+    cudaEvent_t a, b;
+    Events() {
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+    }
+    ~Events() {
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+    }
+    float ms() {
+        float m = 0.f;
+        cudaEventSynchronize(b);
+        cudaEventElapsedTime(&m, a, b);
+        return m;
+    }
+};
+
+double now_s() {
+    return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+int emit(const std::string& s, char* out, size_t cap) {
+    if (s.size() + 1 > cap) return -static_cast<int>(s.size() + 1);
+    std::memcpy(out, s.c_str(), s.size() + 1);
+    return static_cast<int>(s.size());
+}
+
+// Random bf16 query for `batch` sequences on the device.
+void* device_query(std::size_t elems, std::uint32_t seed) {
+    std::vector<bfloat16> h(elems);
+    std::mt19937 rng(seed);
+    std::normal_distribution<float> nd;
+    for (auto& x : h) x = bfloat16(nd(rng));
+    void* d = nullptr;
+    cudaMalloc(&d, elems * 2);
+    cudaMemcpy(d, h.data(), elems * 2, cudaMemcpyHostToDevice);
+    return d;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int qvp_scenario_cow(int prompts, int branches, int prompt_tokens,
+                                                                        int max_append, int seed, int reps,
+                                                                        char* out, size_t cap) {
+    const BlockShape sh = bf16_shape(4);
+    const std::uint32_t T = sh.tokens_per_block;
+    const std::uint32_t per_prompt_blocks = (prompt_tokens + 1 + T - 1) / T;
+    const std::uint32_t pool_blocks =
+        prompts * (per_prompt_blocks + branches * ((max_append + T - 1) / T + 1)) + 64;
+    AllocatorConfig cfg;
+    cfg.block_shape = sh;
+    cfg.max_blocks = pool_blocks;
+    MemoryAllocator alloc(cfg);
+    if (!alloc.has_storage()) return emit("{\"error\": \"pool allocation failed\"}", out, cap);
+    KVCacheManager cache(alloc);
+    std::mt19937 rng(seed);
+    std::uniform_int_distribution<int> append(1, max_append);
+
+    // prompts of prompt_tokens (+1 slot so the first decode token shares the
+    // prompt's last block, which is what copy-on-write must materialise)
+    std::vector<SequenceId> seqs;
+    std::vector<std::uint32_t> ctx;
+    SequenceId next = 1;
+    for (int p = 0; p < prompts; ++p) {
+        const SequenceId root = next++;
+        cache.create_sequence(SequenceMetadata{root, root, {}, {}});
+        cache.reserve_tokens(root, prompt_tokens + 1);
+        seqs.push_back(root);
+        for (int b = 1; b < branches; ++b) {
+            const SequenceId child = next++;
+            cache.fork_sequence(root, SequenceMetadata{child, root, {}, {}});
+            seqs.push_back(child);
+        }
+    }
+    const std::uint64_t copies_before = alloc.copies_done();
+    const double t_host0 = now_s();
+    std::size_t cow_tokens = 0;
+    for (SequenceId s : seqs) {
+        const int n = append(rng);
+        for (int t = 0; t < n; ++t) {
+            const std::uint32_t pos = static_cast<std::uint32_t>(prompt_tokens + t);
+            const auto v = cache.cache_view(s);
+            if (pos >= v->block_table->size() * T) cache.reserve_tokens(s, T);
+            (void)cache.ensure_token_writable(s, pos);
+            ++cow_tokens;
+        }
+        ctx.push_back(static_cast<std::uint32_t>(prompt_tokens + n));
+    }
+    const double host_s = now_s() - t_host0;
+    // the queued copies: one batched launch, timed on the engine stream
+    Events ev;
+    cudaEventRecord(ev.a, alloc.stream());
+    alloc.flush();
+    cudaEventRecord(ev.b, alloc.stream());
+    const float first_ms = ev.ms();
+    const std::uint64_t copies = alloc.copies_done() - copies_before;
+    // the same copies again, `reps` times, for a steady timing
+    std::vector<std::pair<PhysicalBlockId, PhysicalBlockId>> pairs;
+    for (SequenceId s : seqs) {
+        const auto v = cache.cache_view(s);
+        const auto& e = v->block_table->entries()[per_prompt_blocks - 1];
+        const auto root_view = cache.cache_view(((s - 1) / branches) * branches + 1);
+        const PhysicalBlockId src = root_view->block_table->entries()[per_prompt_blocks - 1].physical_id;
+        if (e.physical_id != src) pairs.push_back({src, e.physical_id});
+    }
+    cudaEventRecord(ev.a, alloc.stream());
+    for (int r = 0; r < reps; ++r) {
+        for (auto& pr : pairs) alloc.copy_block(pr.first, pr.second);
+        alloc.flush();
+    }
+    cudaEventRecord(ev.b, alloc.stream());
+    const float copy_ms = ev.ms() / std::max(reps, 1);
+    const double copy_bytes = 2.0 * static_cast<double>(pairs.size()) * alloc.block(0)->size_bytes();
+
+    // decode every branch over its (shared-prefix) table
+    std::vector<CacheView> views;
+    for (SequenceId s : seqs) views.push_back(*cache.cache_view(s));
+    const std::uint32_t hq = 28;
+    const std::size_t qel = seqs.size() * hq * sh.head_dim;
+    void* q = device_query(qel, seed + 1);
+    void* o = nullptr;
+    cudaMalloc(&o, qel * 2);
+    PagedDecodeBatch batch(alloc);
+    const float scale = 1.f / std::sqrt(128.f);
+    for (int w = 0; w < 3; ++w) batch.run(views, ctx, 0, hq, scale, q, o);
+    cudaEventRecord(ev.a, alloc.stream());
+    for (int r = 0; r < reps; ++r) batch.run(views, ctx, 0, hq, scale, q, o);
+    cudaEventRecord(ev.b, alloc.stream());
+    const float dec_ms = ev.ms() / std::max(reps, 1);
+    double logical = 0;
+    for (std::uint32_t c : ctx) logical += 2.0 * c * sh.num_kv_heads * sh.head_dim * 2;
+    const double unique = static_cast<double>(alloc.stats().active_blocks + alloc.stats().shared_blocks) *
+                          alloc.block(0)->size_bytes();
+    const int derr = batch.device_error();
+    cudaFree(q);
+    cudaFree(o);
+
+    std::ostringstream js;
+    js << "{\"workload\": \"cfg3-cow-parallel-sampling\", \"prompts\": " << prompts << ", \"branches\": " << branches
+       << ", \"prompt_tokens\": " << prompt_tokens << ", \"sequences\": " << seqs.size()
+       << ", \"cow_copies\": " << copies << ", \"cow_first_flush_us\": " << first_ms * 1e3
+       << ", \"cow_launch_us\": " << copy_ms * 1e3 << ", \"cow_bytes_rw\": " << copy_bytes
+       << ", \"cow_gbs\": " << copy_bytes / (copy_ms * 1e-3) / 1e9 << ", \"host_bookkeeping_ms\": " << host_s * 1e3
+       << ", \"appended_tokens\": " << cow_tokens << ", \"decode_us\": " << dec_ms * 1e3
+       << ", \"decode_logical_gbs\": " << logical / (dec_ms * 1e-3) / 1e9
+       << ", \"decode_unique_block_gbs\": " << unique / (dec_ms * 1e-3) / 1e9 << ", \"decode_device_error\": " << derr
+       << ", \"decode_ok\": " << (batch.last_status() == 0 ? "true" : "false") << "}";
+    return emit(js.str(), out, cap);
+}
+
+extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uint32_t pool_blocks, double occupancy,
+                                                                         double preempt_fraction, int decode_batch,
+                                                                         int seed, char* out, size_t cap) {
+    const BlockShape sh = bf16_shape(8);
+    AllocatorConfig cfg;
+    cfg.block_shape = sh;
+    cfg.max_blocks = pool_blocks;
+    const double t0 = now_s();
+    MemoryAllocator alloc(cfg);
+    if (!alloc.has_storage()) return emit("{\"error\": \"pool allocation failed: " + alloc.last_error() + "\"}", out, cap);
+    const double pool_s = now_s() - t0;
+    KVCacheManager cache(alloc);
+    std::mt19937 rng(seed);
+    std::uniform_int_distribution<int> ctxd(512, 8192);
+    std::vector<SequenceId> seqs;
+    std::vector<std::uint32_t> ctx;
+    const std::uint32_t target = static_cast<std::uint32_t>(occupancy * pool_blocks);
+    SequenceId next = 1;
+    while (true) {
+        const std::uint32_t c = static_cast<std::uint32_t>(ctxd(rng));
+        const std::uint32_t need = (c + 15) / 16;
+        if (pool_blocks - alloc.stats().free_blocks + need > target) break;
+        cache.create_sequence(SequenceMetadata{next, next, {}, {}});
+        cache.reserve_tokens(next, c);
+        seqs.push_back(next++);
+        ctx.push_back(c);
+    }
+    std::vector<std::size_t> order(seqs.size());
+    for (std::size_t i = 0; i < order.size(); ++i) order[i] = i;
+    std::shuffle(order.begin(), order.end(), rng);
+    const std::size_t n_pre = static_cast<std::size_t>(preempt_fraction * seqs.size());
+    std::vector<std::size_t> pre(order.begin(), order.begin() + n_pre);
+    std::vector<std::size_t> stay(order.begin() + n_pre, order.end());
+    std::size_t pre_blocks = 0;
+    for (std::size_t i : pre) pre_blocks += (ctx[i] + 15) / 16;
+
+    const double t1 = now_s();
+    DeviceSwapBackend swap(alloc, pre_blocks + 16);
+    const double pin_s = now_s() - t1;
+    if (!swap.ready()) return emit("{\"error\": \"pinned slab allocation failed\"}", out, cap);
+    alloc.set_swap_backend(&swap);
+
+    // link peak probe: one 1 GiB pinned copy each way
+    const std::size_t probe = std::min<std::size_t>(std::size_t(1) << 30, pre_blocks * 65536);
+    Events ev;
+    void* hbuf = nullptr;
+    cudaHostAlloc(&hbuf, probe, cudaHostAllocDefault);
+    cudaEventRecord(ev.a, alloc.stream());
+    cudaMemcpyAsync(hbuf, alloc.pool_base(), probe, cudaMemcpyDeviceToHost, alloc.stream());
+    cudaEventRecord(ev.b, alloc.stream());
+    const double d2h_peak = probe / (ev.ms() * 1e-3) / 1e9;
+    cudaEventRecord(ev.a, alloc.stream());
+    cudaMemcpyAsync(alloc.pool_base(), hbuf, probe, cudaMemcpyHostToDevice, alloc.stream());
+    cudaEventRecord(ev.b, alloc.stream());
+    const double h2d_peak = probe / (ev.ms() * 1e-3) / 1e9;
+    cudaFreeHost(hbuf);
+
+    // decode batch over sequences that stay resident
+    const std::uint32_t hq = 64;
+    const int B = std::min<int>(decode_batch, static_cast<int>(stay.size()));
+    std::vector<CacheView> views;
+    std::vector<std::uint32_t> bctx;
+    for (int b = 0; b < B; ++b) bctx.push_back(ctx[stay[b]]);
+    const std::size_t qel = static_cast<std::size_t>(B) * hq * sh.head_dim;
+    void* q = device_query(qel, seed + 3);
+    void* o = nullptr;
+    cudaMalloc(&o, qel * 2);
+    PagedDecodeBatch batch(alloc);
+    auto refresh = [&]() {
+        views.clear();
+        for (int b = 0; b < B; ++b) views.push_back(*cache.cache_view(seqs[stay[b]]));
+    };
+    refresh();
+    for (int w = 0; w < 3; ++w) batch.run(views, bctx, 0, hq, 0.0884f, q, o);
+    cudaEventRecord(ev.a, alloc.stream());
+    for (int r = 0; r < 10; ++r) batch.run(views, bctx, 0, hq, 0.0884f, q, o);
+    cudaEventRecord(ev.b, alloc.stream());
+    const double decode_ms = ev.ms() / 10;
+
+    // swap out: host bookkeeping, then one flush of all moves
+    const double h0 = now_s();
+    std::uint64_t swapped = 0;
+    for (std::size_t i : pre) swapped += cache.swap_out_sequence(seqs[i]);
+    const double out_host_s = now_s() - h0;
+    cudaEventRecord(ev.a, alloc.stream());
+    const double f0 = now_s();
+    alloc.flush();
+    cudaEventRecord(ev.b, alloc.stream());
+    const double out_ms = ev.ms();
+    const double out_wall = now_s() - f0;
+    // a decode step while the swapped quarter is away
+    refresh();
+    batch.run(views, bctx, 0, hq, 0.0884f, q, o);
+    // swap in: bookkeeping, then the flush; then a decode that needs them
+    const double h1 = now_s();
+    bool all_in = true;
+    for (std::size_t i : pre) all_in = cache.swap_in_sequence(seqs[i]) && all_in;
+    const double in_host_s = now_s() - h1;
+    cudaEventRecord(ev.a, alloc.stream());
+    alloc.flush();
+    cudaEventRecord(ev.b, alloc.stream());
+    const double in_ms = ev.ms();
+    // decode stall: a step over resumed sequences issued right after their
+    // swap-in waits for it on the stream; measure issue -> done
+    std::vector<CacheView> rviews;
+    std::vector<std::uint32_t> rctx;
+    for (int b = 0; b < std::min<int>(B, static_cast<int>(pre.size())); ++b) {
+        rviews.push_back(*cache.cache_view(seqs[pre[b]]));
+        rctx.push_back(ctx[pre[b]]);
+    }
+    const double moved = static_cast<double>(swapped) * alloc.block(0)->size_bytes();
+    // decode stall: swap the first resumed batch out again, then issue its
+    // swap-in and a decode over it back to back; the decode waits for the
+    // swap-in on the stream. stall = (swap-in + decode) - decode alone.
+    bool dec_ok = true;
+    float stall_ms = 0.f, rdecode_ms = 0.f;
+    if (!rviews.empty()) {
+        const int R = static_cast<int>(rviews.size());
+        for (int b = 0; b < R; ++b) rviews[b] = *cache.cache_view(seqs[pre[b]]);
+        for (int w = 0; w < 3; ++w) batch.run(rviews, rctx, 0, hq, 0.0884f, q, o);
+        cudaEventRecord(ev.a, alloc.stream());
+        for (int r = 0; r < 10; ++r) batch.run(rviews, rctx, 0, hq, 0.0884f, q, o);
+        cudaEventRecord(ev.b, alloc.stream());
+        rdecode_ms = ev.ms() / 10;
+        for (int b = 0; b < R; ++b) cache.swap_out_sequence(seqs[pre[b]]);
+        alloc.synchronize();
+        cudaEventRecord(ev.a, alloc.stream());
+        for (int b = 0; b < R; ++b) cache.swap_in_sequence(seqs[pre[b]]);
+        for (int b = 0; b < R; ++b) rviews[b] = *cache.cache_view(seqs[pre[b]]);
+        dec_ok = batch.run(rviews, rctx, 0, hq, 0.0884f, q, o);  // flushes the swap-in first
+        cudaEventRecord(ev.b, alloc.stream());
+        stall_ms = ev.ms() - rdecode_ms;
+    }
+    const int derr = batch.device_error();
+    cudaFree(q);
+    cudaFree(o);
+    std::ostringstream js;
+    js << "{\"workload\": \"cfg5-swap-churn\", \"pool_blocks\": " << pool_blocks << ", \"block_bytes\": 65536"
+       << ", \"pool_gib\": " << pool_blocks * 65536.0 / (1 << 30) << ", \"sequences\": " << seqs.size()
+       << ", \"occupied_blocks\": " << pool_blocks - alloc.stats().free_blocks << ", \"preempted_sequences\": "
+       << pre.size() << ", \"swapped_blocks\": " << swapped << ", \"swap_bytes_each_way\": " << moved
+       << ", \"swap_out_ms\": " << out_ms << ", \"swap_out_gbs\": " << moved / (out_ms * 1e-3) / 1e9
+       << ", \"swap_out_flush_wall_ms\": " << out_wall * 1e3 << ", \"swap_out_host_bookkeeping_ms\": "
+       << out_host_s * 1e3 << ", \"swap_in_ms\": " << in_ms << ", \"swap_in_gbs\": " << moved / (in_ms * 1e-3) / 1e9
+       << ", \"swap_in_host_bookkeeping_ms\": " << in_host_s * 1e3 << ", \"all_resumed\": "
+       << (all_in ? "true" : "false") << ", \"pcie_d2h_peak_gbs\": " << d2h_peak << ", \"pcie_h2d_peak_gbs\": "
+       << h2d_peak << ", \"decode_batch\": " << B << ", \"decode_ms\": " << decode_ms
+       << ", \"resume_batch_decode_ms\": " << rdecode_ms << ", \"resume_batch_stall_ms\": " << stall_ms << ", \"resume_batch_sequences\": " << rviews.size()
+       << ", \"pool_alloc_s\": " << pool_s << ", \"slab_pin_s\": " << pin_s << ", \"decode_ok\": "
+       << (dec_ok ? "true" : "false") << ", \"decode_device_error\": " << derr << "}";
+    return emit(js.str(), out, cap);
+}
