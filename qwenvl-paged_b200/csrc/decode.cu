@@ -477,6 +477,12 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     const int nseg = static_cast<int>(p.nseg);
     const uint32_t cap_tokens = p.pitch * 16u;
 
+    // Launched as a programmatic dependent of the previous kernel on the
+    // stream: everything above ran while it drained; wait for it (and its
+    // memory) before reading any input.
+    if (tid == 0) prefetch_tensormap(&tmap);
+    grid_dependency_wait();
+
     // 1. stage counts of every segment, then an inclusive scan (warp 0).
     for (int sg = tid; sg < nseg; sg += kFastThreads) {
         const int c = p.ctx[sg / p.head_groups];
@@ -687,6 +693,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_records(const float* 
     __shared__ float sinv[16];
     constexpr int D4 = D / 4;
     grid_dependency_wait();
+    // the next decode may start its prologue while this grid runs
+    grid_launch_dependents();
     const uint32_t sg = blockIdx.x / HH;
     const int hh = blockIdx.x % HH;
     const int tid = threadIdx.x;
@@ -1054,9 +1062,22 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
     int rc = encode_pool_map(a, HH, &map);
     if (rc != QVP_OK) return rc;
     const uint32_t smem = S::kSmem + (sp.nseg + 1) * 4;
-    kern<<<plan.grid_ctas, kFastThreads, smem, st>>>(map, sp);
-    rc = check_cuda(cudaGetLastError(), "launch stream decode");
-    if (rc != QVP_OK) return rc;
+    {
+        // programmatic dependent of whatever precedes it on the stream (the
+        // previous step's combine): the prologue overlaps that kernel's tail
+        cudaLaunchConfig_t dcfg = {};
+        dcfg.gridDim = dim3(plan.grid_ctas);
+        dcfg.blockDim = dim3(kFastThreads);
+        dcfg.dynamicSmemBytes = smem;
+        dcfg.stream = st;
+        cudaLaunchAttribute dattr[1];
+        dattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        dattr[0].val.programmaticStreamSerializationAllowed = 1;
+        dcfg.attrs = dattr;
+        dcfg.numAttrs = 1;
+        rc = check_cuda(cudaLaunchKernelEx(&dcfg, kern, map, sp), "launch stream decode");
+        if (rc != QVP_OK) return rc;
+    }
 
     // The combine is a programmatic dependent: it may be scheduled while the
     // decode grid still runs and waits (griddepcontrol.wait) for its results.
