@@ -540,8 +540,10 @@ __global__ void __launch_bounds__(kFastThreads, 1)
         int seq = sg / p.head_groups, hg = sg % p.head_groups;
         uint32_t units = (static_cast<uint32_t>(p.ctx[seq]) + 15u) / 16u;
         const int32_t* row = p.tables + static_cast<size_t>(seq) * p.pitch;
+        // two 32-entry windows of the table row: the next one is loaded while
+        // the current one is streamed, so a refill never stalls the producer
         int win = -1;
-        int32_t entry = 0;
+        int32_t entry = 0, entry_next = 0;
         for (uint32_t x = x0; x < x1; ++x) {
             if (x >= seg_end) {
                 do {
@@ -558,9 +560,14 @@ __global__ void __launch_bounds__(kFastThreads, 1)
             const uint32_t it = x - x0;
             const uint32_t slot = it % STAGES;
             const int blk0 = static_cast<int>((x - seg_begin) * J);
-            if (win < 0 || blk0 + J > win + 32) {
+            if (win < 0 || blk0 < win || blk0 + J > win + 64) {
                 win = blk0;
                 entry = (static_cast<uint32_t>(win + lane) < units) ? row[win + lane] : 0;
+                entry_next = (static_cast<uint32_t>(win + 32 + lane) < units) ? row[win + 32 + lane] : 0;
+            } else if (blk0 + J > win + 32) {
+                win += 32;  // J divides 32, so blk0 == win here
+                entry = entry_next;
+                entry_next = (static_cast<uint32_t>(win + 32 + lane) < units) ? row[win + 32 + lane] : 0;
             }
             int32_t ids[J];
 #pragma unroll
@@ -669,18 +676,17 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     flush();
 }
 
-// Partials a (segment, kv head) may have for the one-round-trip merge;
-// segments spread over more CTAs take a loop.
-constexpr int kMergeParts = 16;
 constexpr int kCombineThreads = 256;
+constexpr int kCombineWarps = kCombineThreads / 32;
 
 // Merges the stream-K records of each (segment, kv head) into the output:
-// grid.x = nseg * HH, 256 threads, one float4 of out per thread per pass.
-// Launched as a programmatic dependent of paged_decode_stream; it waits for
-// that grid (griddepcontrol.wait) before reading anything. The (max, sum) of
-// every (row, partial) is fetched in one round trip, turned into normalised
-// weights in shared memory, then each thread issues all its partial loads
-// before summing.
+// grid.x = nseg * HH, 256 threads. Launched as a programmatic dependent of
+// paged_decode_stream; it waits for that grid (griddepcontrol.wait) before
+// reading anything. The eight warps split the segment's partial records
+// (warp w takes partials w, w+8, ...); each lane keeps its share of the
+// G x D outputs in registers and issues all of a partial's loads at once;
+// the warps' sums meet in shared memory. Dynamic shared memory:
+// kCombineWarps * G * D floats.
 template <int D, int HH, int J>
 __global__ void __launch_bounds__(kCombineThreads) combine_records(const float* __restrict__ rec_acc,
                                                                    const float2* __restrict__ rec_ml,
@@ -688,16 +694,17 @@ __global__ void __launch_bounds__(kCombineThreads) combine_records(const float* 
                                                                    __nv_bfloat16* __restrict__ out, uint32_t nseg,
                                                                    uint32_t head_groups, uint32_t hq, uint32_t group,
                                                                    uint32_t grid) {
-    __shared__ float2 sml[16][kMergeParts];
-    __shared__ float sw[16][kMergeParts];
-    __shared__ float sinv[16];
     constexpr int D4 = D / 4;
+    constexpr int kMaxOut = 16 * D4 / 32;  // float4 outputs per lane for G = 16
+    extern __shared__ float4 partial_sums[];  // [warps][G * D4]
+    __shared__ float s_max[kCombineWarps][16];
+    __shared__ float s_sum[kCombineWarps][16];
     grid_dependency_wait();
     // the next decode may start its prologue while this grid runs
     grid_launch_dependents();
     const uint32_t sg = blockIdx.x / HH;
     const int hh = blockIdx.x % HH;
-    const int tid = threadIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t ps = static_cast<uint32_t>(seg_prefix[sg]);
     const uint32_t pe = static_cast<uint32_t>(seg_prefix[sg + 1]);
     const uint32_t total = static_cast<uint32_t>(seg_prefix[nseg]);
@@ -706,88 +713,82 @@ __global__ void __launch_bounds__(kCombineThreads) combine_records(const float* 
     const uint32_t cf = static_cast<uint32_t>((static_cast<uint64_t>(ps + 1) * grid - 1) / total);
     const uint32_t cl = static_cast<uint32_t>((static_cast<uint64_t>(pe) * grid - 1) / total);
     const int G = static_cast<int>(group);
+    const int nout = G * D4;
     const int nparts = static_cast<int>(cl - cf + 1) * J;
     const bool may_be_empty = total < grid;
+    // record of part k: CTA cf + k / J, warp column k % J
+    auto rec_of = [&](int k) { return ((static_cast<size_t>(sg) + cf + k / J) * HH + hh) * J + (k % J); };
+    auto usable = [&](int k) { return !may_be_empty || !cta_is_empty(cf + k / J, total, grid); };
+
+    // per-row maximum over this warp's partials (lane r holds row r)
+    float m = -INFINITY;
+    if (lane < G)
+        for (int k = warp; k < nparts; k += kCombineWarps)
+            if (usable(k)) m = fmaxf(m, rec_ml[rec_of(k) * G + lane].x);
+    if (lane < 16) s_max[warp][lane] = m;
+    __syncthreads();
+    float M = -INFINITY;
+    if (lane < G)
+        for (int w = 0; w < kCombineWarps; ++w) M = fmaxf(M, s_max[w][lane]);
+
+    float4 acc[kMaxOut];
+#pragma unroll
+    for (int i = 0; i < kMaxOut; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lsum = 0.f;
+    for (int k = warp; k < nparts; k += kCombineWarps) {
+        if (!usable(k)) continue;
+        const size_t rec = rec_of(k);
+        // weight of row `lane` in this partial, shared with the warp by shfl
+        float wr = 0.f;
+        if (lane < G) {
+            const float2 ml = rec_ml[rec * G + lane];
+            wr = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+            lsum += wr * ml.y;
+        }
+        const float4* src = reinterpret_cast<const float4*>(rec_acc + rec * G * D);
+        float4 v[kMaxOut];
+#pragma unroll
+        for (int i = 0; i < kMaxOut; ++i) {
+            const int o = lane + 32 * i;
+            if (o < nout) v[i] = src[o];
+        }
+#pragma unroll
+        for (int i = 0; i < kMaxOut; ++i) {
+            const int o = lane + 32 * i;
+            const float w = __shfl_sync(0xffffffffu, wr, (o < nout ? o : 0) / D4);
+            if (o < nout) {
+                acc[i].x += w * v[i].x;
+                acc[i].y += w * v[i].y;
+                acc[i].z += w * v[i].z;
+                acc[i].w += w * v[i].w;
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kMaxOut; ++i) {
+        const int o = lane + 32 * i;
+        if (o < nout) partial_sums[warp * nout + o] = acc[i];
+    }
+    if (lane < 16) s_sum[warp][lane] = lsum;
+    __syncthreads();
     const uint32_t seq = sg / head_groups;
     const uint32_t kvh = (sg % head_groups) * HH + hh;
     __nv_bfloat16* ob = out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kvh) * G) * D;
-    // record of part k (CTA cf + k / J, warp column k % J)
-    auto rec_of = [&](int k) { return ((static_cast<size_t>(sg) + cf + k / J) * HH + hh) * J + (k % J); };
-    auto part_ml = [&](int k, int r) {
-        if (may_be_empty && cta_is_empty(cf + k / J, total, grid)) return make_float2(-INFINITY, 0.f);
-        return rec_ml[rec_of(k) * G + r];
-    };
-
-    if (nparts <= kMergeParts) {
-        for (int i = tid; i < G * nparts; i += kCombineThreads) sml[i / nparts][i % nparts] = part_ml(i % nparts, i / nparts);
-        __syncthreads();
-        if (tid < G) {
-            float M = -INFINITY;
-            for (int k = 0; k < nparts; ++k) M = fmaxf(M, sml[tid][k].x);
-            float L = 0.f;
-            for (int k = 0; k < kMergeParts; ++k) {
-                const float2 ml = k < nparts ? sml[tid][k] : make_float2(-INFINITY, 0.f);
-                const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
-                sw[tid][k] = w;
-                L += w * ml.y;
-            }
-            sinv[tid] = 1.f / L;
+    for (int o = threadIdx.x; o < nout; o += kCombineThreads) {
+        const int r = o / D4;
+        float L = 0.f;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int w = 0; w < kCombineWarps; ++w) {
+            L += s_sum[w][r];
+            const float4 v = partial_sums[w * nout + o];
+            a.x += v.x;
+            a.y += v.y;
+            a.z += v.z;
+            a.w += v.w;
         }
-        __syncthreads();
-        for (int e = tid; e < G * D4; e += kCombineThreads) {
-            const int r = e / D4, d4 = e % D4;
-            float4 v[kMergeParts];
-#pragma unroll
-            for (int k = 0; k < kMergeParts; ++k)
-                if (k < nparts && sw[r][k] != 0.f)
-                    v[k] = reinterpret_cast<const float4*>(rec_acc + (rec_of(k) * G + r) * D)[d4];
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int k = 0; k < kMergeParts; ++k) {
-                const float w = k < nparts ? sw[r][k] : 0.f;
-                if (w != 0.f) {
-                    a.x += w * v[k].x;
-                    a.y += w * v[k].y;
-                    a.z += w * v[k].z;
-                    a.w += w * v[k].w;
-                }
-            }
-            const float inv = sinv[r];
-            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4) = pack_bf16x2(a.x * inv, a.y * inv);
-            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
-        }
-    } else {
-        // a long segment spread over many CTAs: per-row loops
-        if (tid < G) {
-            float M = -INFINITY;
-            for (int k = 0; k < nparts; ++k) M = fmaxf(M, part_ml(k, tid).x);
-            float L = 0.f;
-            for (int k = 0; k < nparts; ++k) {
-                const float2 ml = part_ml(k, tid);
-                if (ml.x != -INFINITY) L += exp2f(ml.x - M) * ml.y;
-            }
-            sw[tid][0] = M;
-            sinv[tid] = 1.f / L;
-        }
-        __syncthreads();
-        for (int e = tid; e < G * D4; e += kCombineThreads) {
-            const int r = e / D4, d4 = e % D4;
-            const float M = sw[r][0];
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int k = 0; k < nparts; ++k) {
-                const float2 ml = part_ml(k, r);
-                if (ml.x == -INFINITY) continue;
-                const float w = exp2f(ml.x - M);
-                const float4 v = reinterpret_cast<const float4*>(rec_acc + (rec_of(k) * G + r) * D)[d4];
-                a.x += w * v.x;
-                a.y += w * v.y;
-                a.z += w * v.z;
-                a.w += w * v.w;
-            }
-            const float inv = sinv[r];
-            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4) = pack_bf16x2(a.x * inv, a.y * inv);
-            *reinterpret_cast<uint32_t*>(ob + r * D + d4 * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
-        }
+        const float inv = 1.f / L;
+        *reinterpret_cast<uint32_t*>(ob + o * 4) = pack_bf16x2(a.x * inv, a.y * inv);
+        *reinterpret_cast<uint32_t*>(ob + o * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
     }
 }
 
@@ -1056,6 +1057,10 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
         int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
                             "cudaFuncSetAttribute(stream decode)");
         if (rc != QVP_OK) return rc;
+        rc = check_cuda(cudaFuncSetAttribute(combine_records<D, HH, J>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kCombineWarps * 16 * D * static_cast<int>(sizeof(float))),
+                        "cudaFuncSetAttribute(combine)");
+        if (rc != QVP_OK) return rc;
         attr_set = true;
     }
     CUtensorMap map;
@@ -1084,7 +1089,7 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(sp.nseg * HH);
     cfg.blockDim = dim3(kCombineThreads);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = static_cast<size_t>(kCombineWarps) * sp.group * D * sizeof(float);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
