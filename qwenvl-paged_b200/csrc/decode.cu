@@ -678,17 +678,19 @@ __global__ void __launch_bounds__(kFastThreads, 1)
 
 constexpr int kCombineThreads = 256;
 constexpr int kCombineWarps = kCombineThreads / 32;
+constexpr int kFewParts = 16;  // partials merged by the one-round-trip path
 
 // Merges the stream-K records of each (segment, kv head) into the output:
 // grid.x = nseg * HH, 256 threads. Launched as a programmatic dependent of
 // paged_decode_stream; it waits for that grid (griddepcontrol.wait) before
 // reading anything. The eight warps split the segment's partial records
-// (warp w takes partials w, w+8, ...); each lane keeps its share of the
+// (warp w takes partials w, w+8, ...) when there are more than kFewParts of
+// them; each lane keeps its share of the
 // G x D outputs in registers and issues all of a partial's loads at once;
 // the warps' sums meet in shared memory. Dynamic shared memory:
 // kCombineWarps * G * D floats.
 template <int D, int HH, int J>
-__global__ void __launch_bounds__(kCombineThreads) combine_records(const float* __restrict__ rec_acc,
+__global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const float* __restrict__ rec_acc,
                                                                    const float2* __restrict__ rec_ml,
                                                                    const int32_t* __restrict__ seg_prefix,
                                                                    __nv_bfloat16* __restrict__ out, uint32_t nseg,
@@ -719,7 +721,62 @@ __global__ void __launch_bounds__(kCombineThreads) combine_records(const float* 
     // record of part k: CTA cf + k / J, warp column k % J
     auto rec_of = [&](int k) { return ((static_cast<size_t>(sg) + cf + k / J) * HH + hh) * J + (k % J); };
     auto usable = [&](int k) { return !may_be_empty || !cta_is_empty(cf + k / J, total, grid); };
+    const uint32_t seq = sg / head_groups;
+    const uint32_t kvh = (sg % head_groups) * HH + hh;
+    __nv_bfloat16* ob = out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kvh) * G) * D;
 
+    if (nparts <= kFewParts) {
+        // Few partials (the common case): every (row, partial) max/sum in
+        // one round trip, normalised weights in shared memory, then each
+        // thread issues all partial loads of one output before summing.
+        __shared__ float2 sml[16][kFewParts];
+        __shared__ float sw[16][kFewParts];
+        __shared__ float sinv[16];
+        for (int i = threadIdx.x; i < G * nparts; i += kCombineThreads) {
+            const int r = i / nparts, k = i % nparts;
+            sml[r][k] = usable(k) ? rec_ml[rec_of(k) * G + r] : make_float2(-INFINITY, 0.f);
+        }
+        __syncthreads();
+        if (threadIdx.x < G) {
+            const int r = threadIdx.x;
+            float M = -INFINITY;
+            for (int k = 0; k < nparts; ++k) M = fmaxf(M, sml[r][k].x);
+            float L = 0.f;
+            for (int k = 0; k < kFewParts; ++k) {
+                const float2 ml = k < nparts ? sml[r][k] : make_float2(-INFINITY, 0.f);
+                const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+                sw[r][k] = w;
+                L += w * ml.y;
+            }
+            sinv[r] = 1.f / L;
+        }
+        __syncthreads();
+        for (int o = threadIdx.x; o < nout; o += kCombineThreads) {
+            const int r = o / D4;
+            float4 v[kFewParts];
+#pragma unroll
+            for (int k = 0; k < kFewParts; ++k)
+                if (k < nparts && sw[r][k] != 0.f)
+                    v[k] = reinterpret_cast<const float4*>(rec_acc + rec_of(k) * G * D)[o];
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < kFewParts; ++k) {
+                const float w = k < nparts ? sw[r][k] : 0.f;
+                if (w != 0.f) {
+                    a.x += w * v[k].x;
+                    a.y += w * v[k].y;
+                    a.z += w * v[k].z;
+                    a.w += w * v[k].w;
+                }
+            }
+            const float inv = sinv[r];
+            *reinterpret_cast<uint32_t*>(ob + o * 4) = pack_bf16x2(a.x * inv, a.y * inv);
+            *reinterpret_cast<uint32_t*>(ob + o * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
+        }
+        return;
+    }
+
+    // Many partials: the warps split them (warp w takes w, w+8, ...).
     // per-row maximum over this warp's partials (lane r holds row r)
     float m = -INFINITY;
     if (lane < G)
@@ -731,49 +788,52 @@ __global__ void __launch_bounds__(kCombineThreads) combine_records(const float* 
     if (lane < G)
         for (int w = 0; w < kCombineWarps; ++w) M = fmaxf(M, s_max[w][lane]);
 
-    float4 acc[kMaxOut];
-#pragma unroll
-    for (int i = 0; i < kMaxOut; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // outputs in chunks of kChunk float4 per lane (all of a partial's loads
+    // for one chunk are issued together)
+    constexpr int kChunk = 8;
     float lsum = 0.f;
-    for (int k = warp; k < nparts; k += kCombineWarps) {
-        if (!usable(k)) continue;
-        const size_t rec = rec_of(k);
-        // weight of row `lane` in this partial, shared with the warp by shfl
-        float wr = 0.f;
-        if (lane < G) {
-            const float2 ml = rec_ml[rec * G + lane];
-            wr = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
-            lsum += wr * ml.y;
-        }
-        const float4* src = reinterpret_cast<const float4*>(rec_acc + rec * G * D);
-        float4 v[kMaxOut];
+    for (int c0 = 0; c0 < kMaxOut; c0 += kChunk) {
+        if (32 * c0 >= nout) break;
+        float4 acc[kChunk];
 #pragma unroll
-        for (int i = 0; i < kMaxOut; ++i) {
-            const int o = lane + 32 * i;
-            if (o < nout) v[i] = src[o];
-        }
+        for (int i = 0; i < kChunk; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int k = warp; k < nparts; k += kCombineWarps) {
+            if (!usable(k)) continue;
+            const size_t rec = rec_of(k);
+            // weight of row `lane` in this partial, shared with the warp by shfl
+            float wr = 0.f;
+            if (lane < G) {
+                const float2 ml = rec_ml[rec * G + lane];
+                wr = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
+                if (c0 == 0) lsum += wr * ml.y;
+            }
+            const float4* src = reinterpret_cast<const float4*>(rec_acc + rec * G * D);
+            float4 v[kChunk];
 #pragma unroll
-        for (int i = 0; i < kMaxOut; ++i) {
-            const int o = lane + 32 * i;
-            const float w = __shfl_sync(0xffffffffu, wr, (o < nout ? o : 0) / D4);
-            if (o < nout) {
-                acc[i].x += w * v[i].x;
-                acc[i].y += w * v[i].y;
-                acc[i].z += w * v[i].z;
-                acc[i].w += w * v[i].w;
+            for (int i = 0; i < kChunk; ++i) {
+                const int o = lane + 32 * (c0 + i);
+                if (o < nout) v[i] = src[o];
+            }
+#pragma unroll
+            for (int i = 0; i < kChunk; ++i) {
+                const int o = lane + 32 * (c0 + i);
+                const float w = __shfl_sync(0xffffffffu, wr, (o < nout ? o : 0) / D4);
+                if (o < nout) {
+                    acc[i].x += w * v[i].x;
+                    acc[i].y += w * v[i].y;
+                    acc[i].z += w * v[i].z;
+                    acc[i].w += w * v[i].w;
+                }
             }
         }
-    }
 #pragma unroll
-    for (int i = 0; i < kMaxOut; ++i) {
-        const int o = lane + 32 * i;
-        if (o < nout) partial_sums[warp * nout + o] = acc[i];
+        for (int i = 0; i < kChunk; ++i) {
+            const int o = lane + 32 * (c0 + i);
+            if (o < nout) partial_sums[warp * nout + o] = acc[i];
+        }
     }
     if (lane < 16) s_sum[warp][lane] = lsum;
     __syncthreads();
-    const uint32_t seq = sg / head_groups;
-    const uint32_t kvh = (sg % head_groups) * HH + hh;
-    __nv_bfloat16* ob = out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kvh) * G) * D;
     for (int o = threadIdx.x; o < nout; o += kCombineThreads) {
         const int r = o / D4;
         float L = 0.f;
