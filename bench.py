@@ -63,7 +63,7 @@ def dist_env():
         os.environ.get("LOCAL_RANK", "0"))
 
 
-def make_workload(name, rank, world, gpus):
+def make_workload(name, rank, world, gpus, args_shard="hybrid"):
     if name == "cfg2":
         # weak scaling: every rank gets the same shape of work (same context
         # lengths); the K/V/Q values differ per rank (device seed below)
@@ -71,8 +71,14 @@ def make_workload(name, rank, world, gpus):
     if name == "cfg1":
         return W.cfg1(seed=1), "weak"
     if name == "cfg4":
-        shards = max(world, 1)
-        return W.cfg4(shards=shards), "strong"
+        if args_shard == "heads":
+            return W.cfg4(shards=max(world, 1)), "strong"
+        # kv heads split while every GPU keeps >= 4 of them, then sequences
+        import sharding
+        hp, dp = sharding.hybrid_grid(8, 32, max(world, 1))
+        w = W.cfg4(shards=hp, batch=32 // dp)
+        w.meta.update({"head_parts": hp, "batch_parts": dp})
+        return w, "strong"
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -139,7 +145,7 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
-    w, scaling = make_workload(args.workload, rank, world, args.gpus)
+    w, scaling = make_workload(args.workload, rank, world, args.gpus, args.shard)
     torch_dtype = torch.bfloat16 if w.dtype == "bf16" else torch.float32
 
     # inputs generated on the device from a seed, resident in HBM
@@ -175,16 +181,21 @@ def run_ours(args):
                    else "paged_decode_generic + combine_partitions")
 
     gather = scaling == "strong" and world > 1 and not args.no_gather
+    hp, dp = w.meta.get("head_parts", world), w.meta.get("batch_parts", 1)
     if gather:
         import sharding
+        g_buf = torch.empty((dp, hp) + tuple(out.shape), dtype=out.dtype, device=dev)
+        g_out = torch.empty((dp * out.shape[0], hp * out.shape[1], out.shape[2]), dtype=out.dtype, device=dev)
 
     def step():
-        st = qvp.decode(a, sh)
+        # the current stream: the caller's, or the capture stream of a graph
+        st = qvp.decode(a, torch.cuda.current_stream().cuda_stream)
         if st != 0:
             raise RuntimeError(f"qvp_decode failed: {st} {qvp.last_error()}")
         if gather:
-            # a consumer that needs every head: all-gather [B, Hq/N, D] (NCCL)
-            sharding.all_gather_heads(out)
+            # a consumer that needs every output on every GPU: one NCCL
+            # all-gather of each rank's [B/dp, Hq/hp, D], reassembled
+            sharding.all_gather_hybrid(out, hp, dp, gathered=g_buf, result=g_out)
 
     def barrier():
         if world > 1:
@@ -208,6 +219,22 @@ def run_ours(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
         return ms
+
+    if gather and args.graph:
+        # One step = decode + all-gather + reorder, a handful of launches a
+        # few tens of microseconds long: capture it once in a CUDA graph and
+        # replay it, so the host does not pace the GPUs.
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+            step()
+        def step():  # noqa: F811
+            graph.replay()
+        graphed = True
+    else:
+        graphed = False
 
     sampler = ClockSampler(local)
     sampler.start()
@@ -283,6 +310,8 @@ def run_ours(args):
             st = qvp.decode(args2[b], sh)
             if st != 0:
                 raise RuntimeError(f"qvp_decode failed: {st} {qvp.last_error()}")
+            if gather:
+                sharding.all_gather_hybrid(dev_out[b], hp, dp, gathered=g_buf, result=g_out)
             ev_dec[b].record(stream)
             down_s.wait_event(ev_dec[b])
             with torch.cuda.stream(down_s):
@@ -324,7 +353,8 @@ def run_ours(args):
             "config": {
                 "workload": w.name,
                 "batch_per_gpu": w.batch,
-                "global_batch": w.batch * (world if scaling == "weak" else 1),
+                "global_batch": w.batch * (world if scaling == "weak" else dp),
+                "cuda_graph": graphed,
                 "context_lens": f"{int(w.context_lens.min())}..{int(w.context_lens.max())} "
                                 f"(sum {int(w.context_lens.sum())})",
                 "heads": f"{w.num_query_heads}q/{w.num_kv_heads}kv per GPU",
@@ -336,9 +366,10 @@ def run_ours(args):
                 "kernel": kernel_name,
                 "l2": f"inputs larger than L2 ({w.kv_bytes() / 1e6:.0f} MB of K/V read per step)",
                 "parallelism": f"dp{world}" if scaling == "weak" else
-                f"kv-head shards x{world}" + (" + NCCL all-gather of outputs" if world > 1 and not args.no_gather else ""),
+                (f"kv-head shards x{w.meta.get('head_parts', world)} x sequence shards x{w.meta.get('batch_parts', 1)}")
+                + (" + NCCL all-gather of outputs" if world > 1 and not args.no_gather else ""),
             },
-            "seqs_per_s": round(w.batch * (world if scaling == "weak" else 1) / (ms_step * 1e-3), 1),
+            "seqs_per_s": round(w.batch * (world if scaling == "weak" else dp) / (ms_step * 1e-3), 1),
             "roofline": {
                 "bound": "hbm",
                 "achieved": round(achieved, 1),
@@ -514,6 +545,10 @@ def main():
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-gather", action="store_true", help="cfg4 shards: skip the output all-gather")
+    p.add_argument("--graph", action="store_true",
+                   help="multi-GPU cfg4: capture decode + all-gather in a CUDA graph (experimental)")
+    p.add_argument("--shard", choices=["hybrid", "heads"], default="hybrid",
+                   help="cfg4 over N GPUs: kv heads only, or kv heads (>= 4 per GPU) then sequences")
     p.add_argument("--profile", action="store_true",
                    help="for ncu: only warm-up and timed decode steps (no clock probe, e2e or CPU baseline)")
     args = p.parse_args()

@@ -14,6 +14,49 @@ from __future__ import annotations
 import numpy as np
 
 
+def hybrid_grid(num_kv_heads: int, batch: int, world: int, min_heads: int = 4):
+    """(head_parts, batch_parts) for `world` ranks: split kv heads while each
+    shard keeps at least `min_heads` of them (a K slice of fewer heads per
+    block streams less efficiently), then split the batch."""
+    hp = 1
+    while hp * 2 <= world and num_kv_heads % (hp * 2) == 0 and num_kv_heads // (hp * 2) >= min_heads:
+        hp *= 2
+    dp = world // hp
+    if hp * dp != world or batch % dp != 0:
+        raise ValueError(f"cannot split {num_kv_heads} kv heads x {batch} sequences over {world} ranks")
+    return hp, dp
+
+
+def hybrid_coords(rank: int, hp: int):
+    """(head part, batch part) of `rank`: ranks of one batch part are adjacent."""
+    return rank % hp, rank // hp
+
+
+def assemble_hybrid(parts, hp: int, dp: int):
+    """Rank-ordered outputs [B/dp, Hq/hp, D] -> [B, Hq, D]."""
+    import torch
+    rows = [torch.cat([parts[d * hp + h] for h in range(hp)], dim=1) for d in range(dp)]
+    return torch.cat(rows, dim=0)
+
+
+def all_gather_hybrid(out_shard, hp: int, dp: int, group=None, gathered=None, result=None):
+    """All-gather of every rank's [B/dp, Hq/hp, D] output, reassembled to
+    [B, Hq, D]: one NCCL all_gather_into_tensor into `gathered` (rank-major
+    [dp, hp, B/dp, Hq/hp, D]) and one reordering copy into `result`. Both
+    buffers are allocated when not given (pass them to keep a step
+    allocation-free, e.g. inside a CUDA graph)."""
+    import torch
+    import torch.distributed as dist
+    b, h, d = out_shard.shape
+    if gathered is None:
+        gathered = torch.empty((dp, hp, b, h, d), dtype=out_shard.dtype, device=out_shard.device)
+    if result is None:
+        result = torch.empty((dp * b, hp * h, d), dtype=out_shard.dtype, device=out_shard.device)
+    dist.all_gather_into_tensor(gathered.view(-1), out_shard.contiguous().view(-1), group=group)
+    result.view(dp, b, hp, h, d).copy_(gathered.permute(0, 2, 1, 3, 4))
+    return result
+
+
 def head_range(num_kv_heads: int, world: int, rank: int):
     if num_kv_heads % world != 0:
         raise ValueError(f"{num_kv_heads} kv heads do not split over {world} ranks")
@@ -57,12 +100,9 @@ def assemble(gathered, axis: int = 1):
     return np.concatenate(list(gathered), axis=axis)
 
 
-def all_gather_heads(out_shard, group=None):
+def all_gather_heads(out_shard, group=None, gathered=None, result=None):
     """torch.distributed all-gather of a rank's [B, Hq/N, D] output, then the
-    head reassembly. Works with NCCL (CUDA tensors) and gloo (CPU tensors)."""
-    import torch
+    head reassembly to [B, Hq, D]. Works with NCCL (CUDA tensors) and gloo
+    (CPU tensors)."""
     import torch.distributed as dist
-    world = dist.get_world_size(group)
-    parts = [torch.empty_like(out_shard) for _ in range(world)]
-    dist.all_gather(parts, out_shard.contiguous(), group=group)
-    return torch.cat(parts, dim=1)
+    return all_gather_hybrid(out_shard, dist.get_world_size(group), 1, group, gathered, result)

@@ -67,3 +67,22 @@ def test_head_range_rejects_uneven_splits():
     assert sharding.head_range(8, 4, 3) == (6, 8)
     with pytest.raises(ValueError):
         sharding.head_range(4, 8, 0)
+
+
+def test_hybrid_grid_keeps_four_heads_per_gpu_then_splits_sequences():
+    assert sharding.hybrid_grid(8, 32, 1) == (1, 1)
+    assert sharding.hybrid_grid(8, 32, 2) == (2, 1)
+    assert sharding.hybrid_grid(8, 32, 4) == (2, 2)
+    assert sharding.hybrid_grid(8, 32, 8) == (2, 4)
+    assert sharding.hybrid_grid(4, 64, 8) == (1, 8)
+
+
+def test_hybrid_assembly_restores_batch_and_head_order():
+    import torch
+    full = torch.arange(8 * 16 * 4, dtype=torch.float32).reshape(8, 16, 4)
+    hp, dp = 2, 4
+    parts = []
+    for r in range(hp * dp):
+        h, d = sharding.hybrid_coords(r, hp)
+        parts.append(full[d * 2:(d + 1) * 2, h * 8:(h + 1) * 8])
+    assert torch.equal(sharding.assemble_hybrid(parts, hp, dp), full)
