@@ -16,6 +16,7 @@
 #include <map>
 #include <optional>
 #include <set>
+#include <string>
 #include <unordered_map>
 #include <vector>
 
@@ -90,6 +91,9 @@ public:
     // Bytes moved between pool and slab so far, in each direction.
     [[nodiscard]] std::uint64_t bytes_out() const noexcept { return bytes_out_; }
     [[nodiscard]] std::uint64_t bytes_in() const noexcept { return bytes_in_; }
+    // Text of the first failure of a flush (empty when every move was
+    // enqueued). A failed store flush loses the bytes of the blocks it held.
+    [[nodiscard]] const std::string& last_error() const noexcept { return error_; }
 
 private:
     struct Move {
@@ -99,6 +103,7 @@ private:
     void flush_stores();
     void flush_loads();
     bool ensure_staging(std::size_t blocks);
+    void note(const std::string& what);  // keeps the first error
 
     MemoryAllocator* allocator_{nullptr};
     std::size_t max_slots_{0};
@@ -118,6 +123,7 @@ private:
     std::vector<std::uint32_t> release_after_flush_;      // slab indices discarded while a load was pending
     std::uint64_t bytes_out_{0};
     std::uint64_t bytes_in_{0};
+    std::string error_;
 };
 
 }  // namespace qwenvl_paged

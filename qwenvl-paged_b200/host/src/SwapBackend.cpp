@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <string>
 
 namespace qwenvl_paged {
 
@@ -91,6 +92,10 @@ DeviceSwapBackend::~DeviceSwapBackend() {
     if (ids_dev_ != nullptr) cudaFree(ids_dev_);
     if (ids_host_ != nullptr) cudaFreeHost(ids_host_);
     if (ids_event_ != nullptr) cudaEventDestroy(static_cast<cudaEvent_t>(ids_event_));
+}
+
+void DeviceSwapBackend::note(const std::string& what) {
+    if (error_.empty()) error_ = what;
 }
 
 bool DeviceSwapBackend::ready() const noexcept { return slab_ != nullptr; }
@@ -196,6 +201,9 @@ void DeviceSwapBackend::flush_stores() {
     OnDevice guard(allocator_->device());
     cudaStream_t st = allocator_->stream();
     if (!ensure_staging(pending_stores_.size())) {
+        // the frames were already handed back to the pool: their bytes are lost
+        note("swap-out: device staging could not be allocated; " + std::to_string(pending_stores_.size()) +
+             " stored blocks were not moved");
         pending_stores_.clear();
         return;
     }
@@ -209,8 +217,9 @@ void DeviceSwapBackend::flush_stores() {
         }
         cudaMemcpyAsync(ids_dev_, ids_host_, n * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
         cudaEventRecord(static_cast<cudaEvent_t>(ids_event_), st);
-        qvp_gather_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(), slot_bytes_,
-                          ids_dev_, static_cast<std::uint32_t>(n), staging_, nullptr, st);
+        if (qvp_gather_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(), slot_bytes_,
+                              ids_dev_, static_cast<std::uint32_t>(n), staging_, nullptr, st) != QVP_OK)
+            note(std::string("swap-out gather: ") + qvp_last_error());
         for_each_run(idx.data(), n, [&](std::size_t first, std::size_t count) {
             cudaMemcpyAsync(slab_ + static_cast<std::size_t>(idx[first]) * slot_bytes_, staging_ + first * slot_bytes_,
                             count * slot_bytes_, cudaMemcpyDeviceToHost, st);
@@ -225,6 +234,8 @@ void DeviceSwapBackend::flush_loads() {
     OnDevice guard(allocator_->device());
     cudaStream_t st = allocator_->stream();
     if (!ensure_staging(pending_loads_.size())) {
+        note("swap-in: device staging could not be allocated; " + std::to_string(pending_loads_.size()) +
+             " loaded blocks were not restored");
         pending_loads_.clear();
         return;
     }
@@ -242,8 +253,9 @@ void DeviceSwapBackend::flush_loads() {
         });
         cudaMemcpyAsync(ids_dev_, ids_host_, n * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
         cudaEventRecord(static_cast<cudaEvent_t>(ids_event_), st);
-        qvp_scatter_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(), slot_bytes_,
-                           ids_dev_, static_cast<std::uint32_t>(n), staging_, nullptr, st);
+        if (qvp_scatter_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(), slot_bytes_,
+                               ids_dev_, static_cast<std::uint32_t>(n), staging_, nullptr, st) != QVP_OK)
+            note(std::string("swap-in scatter: ") + qvp_last_error());
         bytes_in_ += n * slot_bytes_;
     }
     pending_loads_.clear();
