@@ -185,6 +185,42 @@ QVP_API int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream);
 QVP_API int qvp_decode_noalloc(const qvp_decode_args* args, qvp_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * Causal prefill over the paged cache.
+ *
+ * The reference defines prefill as paged_attention_decode<T> applied at every
+ * prompt position p with context_len = p + 1 (PagedAttention.h:43-44). For
+ * each sequence b, the last query_lens[b] tokens of its context_lens[b]-token
+ * cache are queries: query token t (position pos = context_lens[b] -
+ * query_lens[b] + t) attends keys [0, pos] with the decode's arithmetic. K and
+ * V of the new tokens must already be in the cache (qvp_kv_append). query and
+ * out are [batch][max_query_len][num_query_heads][head_dim]; rows t >=
+ * query_lens[b] are neither read nor written. Device-side problems (bad block
+ * ids, lengths outside [1, capacity], query_lens > context_lens or >
+ * max_query_len) set bits in *error_word and never fault.
+ * ------------------------------------------------------------------------- */
+typedef struct qvp_prefill_args {
+    const void* pool;              /* device base of the block pool            */
+    size_t block_stride;           /* bytes between physical blocks            */
+    uint32_t num_blocks;           /* pool capacity in blocks                  */
+    qvp_block_shape shape;         /* shape shared by every block              */
+    int32_t dtype;                 /* qvp_dtype of K/V, query and out          */
+    uint32_t layer;
+    uint32_t num_query_heads;
+    float scale;
+    uint32_t batch;
+    uint32_t max_blocks_per_seq;   /* row pitch of block_tables                */
+    uint32_t max_query_len;        /* token pitch of query / out               */
+    const int32_t* block_tables;   /* device int32 [batch][max_blocks_per_seq] */
+    const int32_t* context_lens;   /* device int32 [batch]: tokens in the cache */
+    const int32_t* query_lens;     /* device int32 [batch]: new tokens (<= ctx) */
+    const void* query;             /* device [batch][max_query_len][Hq][D]     */
+    void* out;                     /* device [batch][max_query_len][Hq][D]     */
+    int32_t* error_word;           /* device int32 or NULL                      */
+} qvp_prefill_args;
+
+QVP_API int qvp_prefill(const qvp_prefill_args* args, qvp_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * Block movers.
  *
  * qvp_copy_blocks: for i < n, copy `bytes` from block pairs[2i] to block

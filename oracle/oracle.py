@@ -156,3 +156,30 @@ class RefDecoder:
 def port_copy_blocks(pool: np.ndarray, block_stride: int, num_blocks: int, nbytes: int, pairs: np.ndarray):
     pairs = np.ascontiguousarray(pairs, dtype=np.int32)
     port_lib().oracle_copy_blocks(_ptr(pool), block_stride, num_blocks, nbytes, _ptr(pairs), len(pairs) // 2)
+
+
+def prefill_pairs(w, query_lens):
+    """(sequence, token) pairs of a prefill and, per pair, the context length
+    the reference would decode with: position + 1 (PagedAttention.h:43-44)."""
+    seq, tok, ctx = [], [], []
+    for b, (c, ql) in enumerate(zip(w.context_lens, query_lens)):
+        for t in range(int(ql)):
+            seq.append(b)
+            tok.append(t)
+            ctx.append(int(c) - int(ql) + t + 1)
+    return np.array(seq, dtype=np.int64), np.array(tok, dtype=np.int64), np.array(ctx, dtype=np.int32)
+
+
+def port_prefill(w, pool, q, query_lens, threads=1):
+    """Prefill as the reference defines it: the decode at every query
+    position. q is [B, max_qlen, Hq, D]; returns float32 [B, max_qlen, Hq, D]
+    (rows past each query length stay zero) and the per-pair status."""
+    seq, tok, ctx = prefill_pairs(w, query_lens)
+    out = np.zeros((w.batch,) + tuple(q.shape[1:]), dtype=np.float32)
+    if len(seq) == 0:
+        return out, np.zeros(0, dtype=np.int32)
+    tables = np.ascontiguousarray(w.tables[seq])
+    qq = np.ascontiguousarray(q[seq, tok])
+    o, status = port_decode(w, pool, qq, threads=threads, context_lens=ctx, tables=tables)
+    out[seq, tok] = o
+    return out, status

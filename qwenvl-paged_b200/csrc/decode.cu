@@ -22,6 +22,7 @@
 //  * paged_decode_generic: any element type, block size, head_dim <= 256 and
 //    group size; one CTA per (sequence, partition, query head), four warps
 //    striding over tokens, lanes over head_dim, exact expf.
+#include "attention_tile.cuh"
 #include "qvp_device.cuh"
 #include "qvp_internal.h"
 
@@ -66,35 +67,6 @@ struct FastShape {
     static constexpr uint32_t kBlock = 2 * kBox;        // K and V
     static constexpr uint32_t kStage = J * kBlock;
     static constexpr uint32_t kSmem = STAGES * kStage + 1024 + 2 * STAGES * 8 + 16;
-};
-
-// Byte address of element chunk `chunk` (8 bf16) of token `t` inside the
-// swizzled box [dh][hh][t][64] written by TMA with 128-byte swizzle.
-__device__ __forceinline__ uint32_t box_addr(uint32_t base, int row_group, int t, int chunk) {
-    const int r = row_group * 16 + t;
-    return base + static_cast<uint32_t>(r * 128 + ((chunk ^ (t & 7)) << 4));
-}
-
-__device__ __forceinline__ uint32_t mask_pair(uint32_t x, int t0, int valid) {
-    const uint32_t lo = (t0 < valid) ? 0x0000FFFFu : 0u;
-    const uint32_t hi = (t0 + 1 < valid) ? 0xFFFF0000u : 0u;
-    return x & (lo | hi);
-}
-
-// Online-softmax state of one consumer warp: query rows g and g+8 of its
-// GQA group (row max in the log2 domain, lane-partial row sums) and the
-// m16n8 accumulator fragments of out[16][D].
-template <int D>
-struct WarpState {
-    float o[D / 8][4];
-    float m0, m1, l0, l1;
-
-    __device__ __forceinline__ void reset() {
-#pragma unroll
-        for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-        m0 = m1 = -INFINITY;
-        l0 = l1 = 0.f;
-    }
 };
 
 // Query rows g and g+8 of the group that reads kv head `kvh` of sequence
@@ -1039,6 +1011,8 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
     return fn;
 }
 
+}  // namespace
+
 // The pool viewed as a 4-D tensor of bf16 so one TMA box is the K (or V)
 // slice of one block for HH consecutive kv heads, laid out in shared memory
 // as [head_dim/64][HH][16 tokens][64]:
@@ -1048,27 +1022,29 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 //   dim3: 64-element half of head_dim    (stride 128 bytes)
 // Token row r of block b, layer l, stream s, slot t is ((b*L + l)*2 + s)*16 + t,
 // which needs blocks stored back to back (stride == byte_size).
-int encode_pool_map(const qvp_decode_args& a, uint32_t hh, CUtensorMap* map) {
+
+int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape& shape, uint32_t hh,
+                    CUtensorMap* map) {
     struct Key {
         const void* pool;
         uint32_t num_blocks, layers, heads, dim, hh;
     };
     static thread_local Key last{};
     static thread_local CUtensorMap cached;
-    const Key key{a.pool, a.num_blocks, a.shape.num_layers, a.shape.num_kv_heads, a.shape.head_dim, hh};
+    const Key key{pool, num_blocks, shape.num_layers, shape.num_kv_heads, shape.head_dim, hh};
     if (std::memcmp(&key, &last, sizeof(Key)) == 0) {
         *map = cached;
         return QVP_OK;
     }
     auto encode = get_encode_fn();
     if (encode == nullptr) return fail(QVP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-    const uint32_t D = a.shape.head_dim;
-    const uint32_t H = a.shape.num_kv_heads;
-    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(a.num_blocks) * a.shape.num_layers * 2 * 16, H, D / 64};
+    const uint32_t D = shape.head_dim;
+    const uint32_t H = shape.num_kv_heads;
+    cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(num_blocks) * shape.num_layers * 2 * 16, H, D / 64};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(H) * D * 2, static_cast<cuuint64_t>(D) * 2, 128};
     cuuint32_t box[4] = {64, 16, hh, D / 64};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(a.pool), dims, strides, box,
+    CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(pool), dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(QVP_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", int(r));
@@ -1076,6 +1052,8 @@ int encode_pool_map(const qvp_decode_args& a, uint32_t hh, CUtensorMap* map) {
     cached = *map;
     return QVP_OK;
 }
+
+namespace {
 
 template <int D, int HH, int STAGES>
 int launch_fast_t(const qvp_decode_args& a, const DecodePlan& plan, const FastParams& fp, cudaStream_t st) {
@@ -1089,7 +1067,7 @@ int launch_fast_t(const qvp_decode_args& a, const DecodePlan& plan, const FastPa
         attr_set = true;
     }
     CUtensorMap map;
-    int rc = encode_pool_map(a, HH, &map);
+    int rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
     if (rc != QVP_OK) return rc;
     dim3 grid(plan.max_splits, a.shape.num_kv_heads / HH, a.batch);
     kern<<<grid, kFastThreads, S::kSmem, st>>>(map, fp);
@@ -1124,7 +1102,7 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
         attr_set = true;
     }
     CUtensorMap map;
-    int rc = encode_pool_map(a, HH, &map);
+    int rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
     if (rc != QVP_OK) return rc;
     const uint32_t smem = S::kSmem + (sp.nseg + 1) * 4;
     {

@@ -76,6 +76,28 @@ class DecodeArgs(C.Structure):
     ]
 
 
+class PrefillArgs(C.Structure):
+    _fields_ = [
+        ("pool", C.c_void_p),
+        ("block_stride", C.c_size_t),
+        ("num_blocks", C.c_uint32),
+        ("shape", BlockShape),
+        ("dtype", C.c_int32),
+        ("layer", C.c_uint32),
+        ("num_query_heads", C.c_uint32),
+        ("scale", C.c_float),
+        ("batch", C.c_uint32),
+        ("max_blocks_per_seq", C.c_uint32),
+        ("max_query_len", C.c_uint32),
+        ("block_tables", C.c_void_p),
+        ("context_lens", C.c_void_p),
+        ("query_lens", C.c_void_p),
+        ("query", C.c_void_p),
+        ("out", C.c_void_p),
+        ("error_word", C.c_void_p),
+    ]
+
+
 def _load() -> C.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
@@ -101,6 +123,7 @@ def _load() -> C.CDLL:
         "qvp_decode_plan": (C.c_int, [P(DecodeArgs), P(u32), P(u32), P(C.c_int)]),
         "qvp_decode": (C.c_int, [P(DecodeArgs), vp]),
         "qvp_decode_noalloc": (C.c_int, [P(DecodeArgs), vp]),
+        "qvp_prefill": (C.c_int, [P(PrefillArgs), vp]),
         "qvp_copy_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp]),
         "qvp_gather_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
         "qvp_scatter_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
@@ -121,7 +144,7 @@ EXPORTED = [
     "qvp_block_bytes", "qvp_block_stride", "qvp_last_error", "qvp_version", "qvp_device_sm_count",
     "qvp_pool_create", "qvp_pool_destroy", "qvp_pool_base", "qvp_pool_stride", "qvp_pool_num_blocks",
     "qvp_pool_device", "qvp_pool_write", "qvp_pool_read", "qvp_decode_workspace_size",
-    "qvp_decode_plan", "qvp_decode", "qvp_decode_noalloc", "qvp_copy_blocks", "qvp_gather_blocks", "qvp_scatter_blocks",
+    "qvp_decode_plan", "qvp_decode", "qvp_decode_noalloc", "qvp_prefill", "qvp_copy_blocks", "qvp_gather_blocks", "qvp_scatter_blocks",
     "qvp_kv_append",
 ]
 
