@@ -15,6 +15,7 @@
 //   create s | fork p c | reserve s n | write s pos | swapout s | swapin s
 //   release s | view s | alloc | rel id | retain id | copy a b
 //   bswapout id | bswapin slot | discard slot
+//   failstore n | failload n        (the swap backend fails its nth next store / load)
 //   enqueue r s prompt | schedule | complete r | cancel r | preempt r | resume r
 #pragma once
 
@@ -33,6 +34,30 @@ namespace replay {
 
 namespace qp = qwenvl_paged;
 
+// Fault injection: a swap backend that forwards to another one but fails its
+// Nth store or load from the moment it is armed (then behaves again).
+class FailingSwapBackend final : public qp::SwapBackend {
+public:
+    explicit FailingSwapBackend(qp::SwapBackend& inner) : inner_(inner) {}
+    std::optional<qp::SwapSlotId> store(const qp::PhysicalBlock& block) override {
+        if (store_countdown_ > 0 && --store_countdown_ == 0) return std::nullopt;
+        return inner_.store(block);
+    }
+    bool load(qp::SwapSlotId slot, qp::PhysicalBlock& block) override {
+        if (load_countdown_ > 0 && --load_countdown_ == 0) return false;
+        return inner_.load(slot, block);
+    }
+    void discard(qp::SwapSlotId slot) override { inner_.discard(slot); }
+    std::size_t resident_slots() const noexcept override { return inner_.resident_slots(); }
+    void fail_store(int nth) { store_countdown_ = nth; }
+    void fail_load(int nth) { load_countdown_ = nth; }
+
+private:
+    qp::SwapBackend& inner_;
+    int store_countdown_ = 0;
+    int load_countdown_ = 0;
+};
+
 template <typename Opt>
 std::string show(const Opt& o) {
     std::ostringstream s;
@@ -47,6 +72,7 @@ inline std::string run(const std::string& script) {
     std::istringstream in(script);
     std::ostringstream out;
     std::unique_ptr<qp::HostSwapBackend> swap;
+    std::unique_ptr<FailingSwapBackend> faulty;
     std::unique_ptr<qp::MemoryAllocator> alloc;
     std::unique_ptr<qp::KVCacheManager> cache;
     std::unique_ptr<qp::Scheduler> sched;
@@ -105,9 +131,11 @@ inline std::string run(const std::string& script) {
             cache.reset();
             alloc.reset(REPLAY_MAKE_ALLOCATOR(cfg));
             swap.reset();
+            faulty.reset();
             if (slots >= 0) {
                 swap = std::make_unique<qp::HostSwapBackend>(static_cast<std::size_t>(slots));
-                alloc->set_swap_backend(swap.get());
+                faulty = std::make_unique<FailingSwapBackend>(*swap);
+                alloc->set_swap_backend(faulty.get());
             }
             cache = std::make_unique<qp::KVCacheManager>(*alloc);
             qp::SchedulerConfig sc;
@@ -201,6 +229,16 @@ inline std::string run(const std::string& script) {
             t >> slot;
             alloc->discard_swapped(slot);
             out << " done\n";
+        } else if (op == "failstore" && faulty) {
+            int k;
+            t >> k;
+            faulty->fail_store(k);
+            out << " armed\n";
+        } else if (op == "failload" && faulty) {
+            int k;
+            t >> k;
+            faulty->fail_load(k);
+            out << " armed\n";
         } else if (op == "enqueue" && sched) {
             qp::Request r;
             t >> r.request_id >> r.root_sequence_id >> r.prompt_tokens;

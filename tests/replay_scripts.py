@@ -37,8 +37,8 @@ def random_script(seed: int, n_ops: int = 160, scheduler: bool = False) -> str:
                 lines.append(f"{op} {r}")
             continue
         op = rng.choices(["create", "fork", "reserve", "write", "swapout", "swapin", "release", "view", "alloc",
-                          "rel", "retain", "copy", "bswapout", "bswapin", "discard"],
-                         weights=[8, 6, 12, 12, 5, 5, 5, 3, 4, 4, 3, 2, 3, 3, 2])[0]
+                          "rel", "retain", "copy", "bswapout", "bswapin", "discard", "failstore", "failload"],
+                         weights=[8, 6, 12, 12, 5, 5, 5, 3, 4, 4, 3, 2, 3, 3, 2, 1, 1])[0]
         s = rng.choice(seqs)
         if op in ("create", "swapout", "swapin", "release", "view"):
             lines.append(f"{op} {s}")
@@ -50,6 +50,8 @@ def random_script(seed: int, n_ops: int = 160, scheduler: bool = False) -> str:
             lines.append(f"write {s} {rng.randint(0, 6 * T)}")
         elif op == "alloc":
             lines.append("alloc")
+        elif op in ("failstore", "failload"):
+            lines.append(f"{op} {rng.randint(1, 4)}")
         elif op in ("rel", "retain", "bswapout"):
             lines.append(f"{op} {rng.randint(0, blocks)}")
         elif op == "copy":
@@ -80,6 +82,15 @@ HANDWRITTEN = {
     # scheduler: memory pressure keeps requests pending, watermark preempts newest
     "scheduler_watermark": "init 4 1 1 4 4 6 16 3 24 2\nenqueue 1 101 8\nenqueue 2 102 8\nschedule\ncomplete 1\n"
                            "complete 2\nenqueue 3 103 8\nschedule\nschedule\nresume 2\ncancel 1\nresume 2\nschedule\n",
+    # fault injection: a store fails in the middle of a sequence swap-out (the
+    # rest still move), a load fails in the middle of a swap-in (the frame is
+    # released, generation advances, the sequence stays partly swapped)
+    "swap_store_failure_mid_sequence": "init 4 1 1 4 4 8 8\ncreate 1\nreserve 1 16\nfailstore 2\nswapout 1\n"
+                                       "view 1\nswapin 1\nview 1\n",
+    "swap_load_failure_mid_sequence": "init 4 1 1 4 4 8 8\ncreate 1\nreserve 1 16\nswapout 1\nfailload 3\n"
+                                      "swapin 1\nview 1\nswapin 1\nview 1\nrelease 1\n",
+    "preempt_with_failing_store": "init 4 1 1 4 4 6 16 3 24 0\nenqueue 1 101 8\nenqueue 2 102 8\nschedule\n"
+                                  "failstore 1\npreempt 2\nresume 2\nfailload 1\npreempt 1\nresume 1\nresume 1\n",
     "scheduler_no_backend": "init 4 1 1 4 4 4 -1 4 100 1\nenqueue 1 101 12\nenqueue 2 102 8\nschedule\n"
                             "complete 1\nschedule\npreempt 1\nresume 1\ncancel 2\nschedule\n",
 }

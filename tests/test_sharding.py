@@ -86,3 +86,38 @@ def test_hybrid_assembly_restores_batch_and_head_order():
         h, d = sharding.hybrid_coords(r, hp)
         parts.append(full[d * 2:(d + 1) * 2, h * 8:(h + 1) * 8])
     assert torch.equal(sharding.assemble_hybrid(parts, hp, dp), full)
+
+
+def _dying_rank_main(rank, world, port, result):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=4))
+    if rank == 1:
+        # leaves between steps, with nothing in flight
+        os._exit(0)
+    try:
+        sharding.all_gather_heads(torch.zeros(2, 4, 8))
+        result[rank] = "no error"
+    except Exception as e:  # the survivor's collective ends with an error, not a hang
+        result[rank] = type(e).__name__
+
+
+def test_a_rank_that_leaves_makes_the_next_gather_fail_instead_of_hanging():
+    import multiprocessing as mpx
+    import time
+    port = _free_port()
+    mgr = mp.Manager()
+    result = mgr.dict()
+    ctx = mpx.get_context("spawn")
+    procs = [ctx.Process(target=_dying_rank_main, args=(r, 2, port, result)) for r in range(2)]
+    t0 = time.time()
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    assert all(not p.is_alive() for p in procs)
+    assert result.get(0) not in (None, "no error")
+    assert time.time() - t0 < 60
