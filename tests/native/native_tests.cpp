@@ -17,6 +17,8 @@
 
 #include <cuda_runtime.h>
 
+#include "harness.h"
+
 #include <cmath>
 #include <cstring>
 #include <functional>
@@ -28,40 +30,6 @@
 using namespace qwenvl_paged;
 
 namespace {
-
-struct Failure {
-    std::string what;
-};
-
-#define CHECK(cond)                                                                      \
-    do {                                                                                 \
-        if (!(cond)) throw Failure{std::string(__FILE__ ":") + std::to_string(__LINE__) + \
-                                   ": " #cond};                                          \
-    } while (0)
-
-#define CHECK_NEAR(a, b, tol)                                                                       \
-    do {                                                                                            \
-        const double a_ = (a), b_ = (b);                                                            \
-        if (!(std::fabs(a_ - b_) <= (tol))) {                                                       \
-            std::ostringstream s_;                                                                  \
-            s_ << __FILE__ << ":" << __LINE__ << ": " << a_ << " vs " << b_ << " (" #a " ~ " #b ")"; \
-            throw Failure{s_.str()};                                                                \
-        }                                                                                           \
-    } while (0)
-
-std::map<std::string, std::function<void()>>& registry() {
-    static std::map<std::string, std::function<void()>> r;
-    return r;
-}
-
-struct Register {
-    Register(const char* name, std::function<void()> fn) { registry()[name] = std::move(fn); }
-};
-
-#define NATIVE_TEST(name)                                  \
-    void name();                                           \
-    const Register reg_##name(#name, name);                \
-    void name()
 
 BlockShape shape_of(std::uint32_t tpb, std::uint32_t layers, std::uint32_t heads, std::uint32_t dim,
                     std::uint32_t elem = 4) {
@@ -522,28 +490,9 @@ NATIVE_TEST(end_to_end_scheduler_prefill_decode_preempt_resume) {
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) int qvp_native_list(char* out, size_t cap) {
-    std::string names;
-    for (const auto& kv : registry()) names += kv.first + "\n";
-    if (names.size() + 1 > cap) return -1;
-    std::memcpy(out, names.c_str(), names.size() + 1);
-    return static_cast<int>(registry().size());
+    return native::list_cases(out, cap);
 }
 
 extern "C" __attribute__((visibility("default"))) int qvp_native_run(const char* name, char* msg, size_t cap) {
-    const auto it = registry().find(name);
-    std::string text;
-    int rc = 0;
-    if (it == registry().end()) {
-        text = "unknown test";
-        rc = 2;
-    } else {
-        try {
-            it->second();
-        } catch (const Failure& f) {
-            text = f.what;
-            rc = 1;
-        }
-    }
-    std::snprintf(msg, cap, "%s", text.c_str());
-    return rc;
+    return native::run_case(name, msg, cap);
 }
