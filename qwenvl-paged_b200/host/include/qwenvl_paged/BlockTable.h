@@ -3,11 +3,18 @@
 // sorted by logical index, lookup misses on a swapped entry, fork clears
 // `writable`. `entries()` order is what a batch step flattens into the device
 // int32 tables.
+//
+// Beyond the reference interface, revision() stamps the table's contents: a
+// process-wide counter value taken at construction and at every call that can
+// change a mapping (map, unmap, set_writable, mutable_entry, fork). Two table
+// states with the same stamp hold the same entries, so a device-resident copy
+// of the table can be refreshed only when the stamp moves.
 #pragma once
 
 #include "qwenvl_paged/Block.h"
 
 #include <cstddef>
+#include <cstdint>
 #include <optional>
 #include <vector>
 
@@ -25,6 +32,10 @@ struct BlockTableEntry {
 class BlockTable {
 public:
     explicit BlockTable(SequenceId sequence_id, CacheKind cache_kind = CacheKind::TextKV);
+    BlockTable(const BlockTable&) = default;
+    BlockTable& operator=(const BlockTable&) = default;
+    BlockTable(BlockTable&& other) noexcept;
+    BlockTable& operator=(BlockTable&& other) noexcept;
 
     [[nodiscard]] SequenceId sequence_id() const noexcept;
     [[nodiscard]] CacheKind cache_kind() const noexcept;
@@ -39,6 +50,7 @@ public:
     void set_writable(LogicalBlockIndex index, bool writable);
     [[nodiscard]] const std::vector<BlockTableEntry>& entries() const noexcept;
     [[nodiscard]] BlockTable fork(SequenceId child_sequence_id) const;
+    [[nodiscard]] std::uint64_t revision() const noexcept;
 
 private:
     // Position of the first entry whose logical index is >= `index`.
@@ -47,6 +59,7 @@ private:
     SequenceId sequence_id_{0};
     CacheKind cache_kind_{CacheKind::TextKV};
     std::vector<BlockTableEntry> entries_;
+    std::uint64_t revision_{0};
 };
 
 }  // namespace qwenvl_paged

@@ -12,12 +12,16 @@
 
 #include "qwenvl_paged/CacheLayout.h"
 #include "qwenvl_paged/KVCacheManager.h"
+#include "qwenvl_paged/ResidentTables.h"
 
 #include <cstddef>
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <vector>
+
+struct qvp_decode_args;  // include/qvp.h
 
 namespace qwenvl_paged {
 
@@ -68,9 +72,15 @@ template <typename T>
 // launches qvp_decode on the allocator's stream. `query` and `out` are device
 // arrays [batch][num_query_heads][head_dim] in the pool's element type.
 // Buffers are kept and reused across calls.
+//
+// With resident_tables the tables stay on the device between calls
+// (ResidentBlockTables): a call uploads the context lengths and only the rows
+// whose BlockTable changed, which an engine gets by keeping each sequence at
+// the same batch position from step to step. The checks and the results are
+// the same as without it.
 class PagedDecodeBatch {
 public:
-    explicit PagedDecodeBatch(const MemoryAllocator& allocator);
+    explicit PagedDecodeBatch(const MemoryAllocator& allocator, bool resident_tables = false);
     ~PagedDecodeBatch();
     PagedDecodeBatch(const PagedDecodeBatch&) = delete;
     PagedDecodeBatch& operator=(const PagedDecodeBatch&) = delete;
@@ -83,9 +93,15 @@ public:
     [[nodiscard]] const std::string& last_error() const noexcept { return error_; }
     // Device error bits (qvp_decode error_word) of the last run; waits for it.
     [[nodiscard]] int device_error();
+    // Table rows and bytes the last run sent to the device (all rows unless
+    // the tables are resident).
+    [[nodiscard]] std::uint32_t rows_uploaded() const noexcept { return rows_uploaded_; }
+    [[nodiscard]] std::size_t bytes_uploaded() const noexcept { return bytes_uploaded_; }
 
 private:
     bool grow(std::size_t table_ints, std::size_t batch, std::size_t workspace);
+    bool run_resident(const std::vector<CacheView>& views, const std::vector<std::uint32_t>& context_lens,
+                      ::qvp_decode_args& a, std::uint32_t max_ctx, const void* query, void* out);
 
     const MemoryAllocator* allocator_;
     std::int32_t* host_buf_{nullptr};    // pinned: tables then context lengths
@@ -95,6 +111,9 @@ private:
     std::size_t workspace_bytes_{0};
     std::int32_t* error_word_{nullptr};
     void* upload_event_{nullptr};
+    std::unique_ptr<ResidentBlockTables> resident_;
+    std::uint32_t rows_uploaded_{0};
+    std::size_t bytes_uploaded_{0};
     int status_{0};
     std::string error_;
 };

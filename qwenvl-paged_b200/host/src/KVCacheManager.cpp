@@ -71,10 +71,15 @@ std::optional<PhysicalBlockId> KVCacheManager::ensure_token_writable(SequenceId 
     if (table.empty()) return std::nullopt;
     const std::uint32_t tpb = table.entries().front().logical.token_count;
     if (tpb == 0) return std::nullopt;
-    BlockTableEntry* e = table.mutable_entry(static_cast<LogicalBlockIndex>(token_position / tpb));
-    if (e == nullptr || e->swap_slot.has_value()) return std::nullopt;
-    const PhysicalBlockInfo* in = allocator_->info(e->physical_id);
+    const LogicalBlockIndex index = static_cast<LogicalBlockIndex>(token_position / tpb);
+    const BlockTableEntry* seen = table.entry(index);
+    if (seen == nullptr || seen->swap_slot.has_value()) return std::nullopt;
+    const PhysicalBlockInfo* in = allocator_->info(seen->physical_id);
     if (in == nullptr) return std::nullopt;
+    // the common decode case: a private, writable block leaves the table (and
+    // its revision stamp) untouched
+    if (in->ref_count <= 1 && seen->writable) return seen->physical_id;
+    BlockTableEntry* e = table.mutable_entry(index);
     if (in->ref_count <= 1) {
         e->writable = true;
         return e->physical_id;

@@ -185,7 +185,9 @@ bool decode_one(const CacheView& view, const void* query, std::size_t elem_bytes
 
 }  // namespace detail
 
-PagedDecodeBatch::PagedDecodeBatch(const MemoryAllocator& allocator) : allocator_(&allocator) {}
+PagedDecodeBatch::PagedDecodeBatch(const MemoryAllocator& allocator, bool resident_tables)
+    : allocator_(&allocator),
+      resident_(resident_tables ? std::make_unique<ResidentBlockTables>(allocator) : nullptr) {}
 
 PagedDecodeBatch::~PagedDecodeBatch() {
     OnDevice guard(allocator_->device());
@@ -261,6 +263,7 @@ bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vecto
     OnDevice guard(alloc.device());
     qvp_decode_args a = base_args(alloc, elem, layer, num_query_heads, scale);
     a.batch = static_cast<std::uint32_t>(B);
+    if (resident_) return run_resident(views, context_lens, a, max_ctx, query, out);
     a.max_blocks_per_seq = pitch;
     a.max_context_len = max_ctx;
     a.block_tables = reinterpret_cast<const std::int32_t*>(0x10);
@@ -297,12 +300,56 @@ bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vecto
     cudaStream_t st = alloc.stream();
     cudaMemcpyAsync(dev_buf_, host_buf_, ints * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
     cudaEventRecord(static_cast<cudaEvent_t>(upload_event_), st);
+    rows_uploaded_ = static_cast<std::uint32_t>(B);
+    bytes_uploaded_ = ints * sizeof(std::int32_t);
     a.block_tables = dev_buf_;
     a.context_lens = dev_buf_ + B * pitch;
     a.workspace = ws ? workspace_ : nullptr;
     a.workspace_bytes = ws ? workspace_bytes_ : 0;
     a.error_word = error_word_;
     status_ = qvp_decode(&a, st);
+    if (status_ != QVP_OK) error_ = qvp_last_error();
+    return status_ == QVP_OK;
+}
+
+// run() with resident tables: the rows go up first (they fix the pitch the
+// workspace size depends on), then copy-on-write copies, then the decode.
+bool PagedDecodeBatch::run_resident(const std::vector<CacheView>& views, const std::vector<std::uint32_t>& context_lens,
+                                    qvp_decode_args& a, std::uint32_t max_ctx, const void* query, void* out) {
+    MemoryAllocator& alloc = const_cast<MemoryAllocator&>(*allocator_);
+    if (!grow(0, views.size(), 0)) {
+        status_ = QVP_ERR_NOMEM;
+        error_ = "could not allocate decode buffers";
+        return false;
+    }
+    if (!resident_->update(views, context_lens, error_word_, &error_)) {
+        status_ = resident_->status();
+        return false;
+    }
+    rows_uploaded_ = resident_->rows_written();
+    bytes_uploaded_ = resident_->bytes_uploaded();
+    a.max_blocks_per_seq = resident_->pitch();
+    a.max_context_len = max_ctx;
+    a.block_tables = resident_->device_tables();
+    a.context_lens = resident_->device_context_lens();
+    a.query = query;
+    a.out = out;
+    std::size_t ws = 0;
+    status_ = qvp_decode_workspace_size(&a, &ws);
+    if (status_ != QVP_OK) {
+        error_ = qvp_last_error();
+        return false;
+    }
+    if (!grow(0, views.size(), ws)) {
+        status_ = QVP_ERR_NOMEM;
+        error_ = "could not allocate decode workspace";
+        return false;
+    }
+    alloc.flush();  // queued copy-on-write copies and swap moves land first
+    a.workspace = ws ? workspace_ : nullptr;
+    a.workspace_bytes = ws ? workspace_bytes_ : 0;
+    a.error_word = error_word_;
+    status_ = qvp_decode(&a, alloc.stream());
     if (status_ != QVP_OK) error_ = qvp_last_error();
     return status_ == QVP_OK;
 }
