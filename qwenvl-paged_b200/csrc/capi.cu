@@ -26,9 +26,21 @@ int check_cuda(cudaError_t err, const char* what) {
     return fail(QVP_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
 }
 
+int set_smem_limit_once(std::atomic<std::uint64_t>& done, const void* func, int bytes, const char* what) {
+    int dev = 0;
+    const int rc = check_cuda(cudaGetDevice(&dev), what);
+    if (rc != QVP_OK) return rc;
+    const std::uint64_t bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+    if (bit != 0 && (done.load(std::memory_order_acquire) & bit) != 0) return QVP_OK;
+    const int set = check_cuda(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes), what);
+    if (set == QVP_OK && bit != 0) done.fetch_or(bit, std::memory_order_release);
+    return set;
+}
+
+// Cached per thread (a thread's current device rarely changes).
 int device_sm_count() {
-    static int cached_dev = -2;
-    static int cached = 0;
+    static thread_local int cached_dev = -2;
+    static thread_local int cached = 0;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         cudaGetLastError();

@@ -995,19 +995,19 @@ __global__ void combine_partitions(const float* __restrict__ ws_o, const float2*
 
 // ---- host side ------------------------------------------------------------
 
+// Looked up once per process (a function-local static is initialised once,
+// thread-safely).
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static bool tried = false;
-    if (!tried) {
-        tried = true;
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
         void* ptr = nullptr;
         cudaDriverEntryPointQueryResult qres;
         if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault,
                                              &qres) == cudaSuccess &&
-            qres == cudaDriverEntryPointSuccess) {
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-        }
-    }
+            qres == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+        cudaGetLastError();
+        return static_cast<PFN_cuTensorMapEncodeTiled_v12000>(nullptr);
+    }();
     return fn;
 }
 
@@ -1031,7 +1031,15 @@ int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape
     };
     static thread_local Key last{};
     static thread_local CUtensorMap cached;
-    const Key key{pool, num_blocks, shape.num_layers, shape.num_kv_heads, shape.head_dim, hh};
+    // compared with memcmp, so the padding bytes are zeroed too
+    Key key;
+    std::memset(&key, 0, sizeof(key));
+    key.pool = pool;
+    key.num_blocks = num_blocks;
+    key.layers = shape.num_layers;
+    key.heads = shape.num_kv_heads;
+    key.dim = shape.head_dim;
+    key.hh = hh;
     if (std::memcmp(&key, &last, sizeof(Key)) == 0) {
         *map = cached;
         return QVP_OK;
@@ -1058,16 +1066,13 @@ namespace {
 template <int D, int HH, int STAGES>
 int launch_fast_t(const qvp_decode_args& a, const DecodePlan& plan, const FastParams& fp, cudaStream_t st) {
     using S = FastShape<D, HH, STAGES>;
-    static bool attr_set = false;
+    static std::atomic<std::uint64_t> attr_done{0};
     auto kern = paged_decode_fast<D, HH, STAGES>;
-    if (!attr_set) {
-        int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
-                            "cudaFuncSetAttribute(fast decode)");
-        if (rc != QVP_OK) return rc;
-        attr_set = true;
-    }
+    int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern), S::kSmem,
+                                 "cudaFuncSetAttribute(fast decode)");
+    if (rc != QVP_OK) return rc;
     CUtensorMap map;
-    int rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
+    rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
     if (rc != QVP_OK) return rc;
     dim3 grid(plan.max_splits, a.shape.num_kv_heads / HH, a.batch);
     kern<<<grid, kFastThreads, S::kSmem, st>>>(map, fp);
@@ -1089,20 +1094,16 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
     constexpr int J = S::J;
     constexpr uint32_t kMaxSmem = S::kSmem + (kStreamMaxSegments + 1) * 4;
     static_assert(kMaxSmem <= 232448, "stream decode exceeds the 227 KB shared-memory limit");
-    static bool attr_set = false;
+    static std::atomic<std::uint64_t> attr_done{0}, combine_attr_done{0};
     auto kern = paged_decode_stream<D, HH, STAGES>;
-    if (!attr_set) {
-        int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem),
-                            "cudaFuncSetAttribute(stream decode)");
-        if (rc != QVP_OK) return rc;
-        rc = check_cuda(cudaFuncSetAttribute(combine_records<D, HH, J>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kCombineWarps * 16 * D * static_cast<int>(sizeof(float))),
-                        "cudaFuncSetAttribute(combine)");
-        if (rc != QVP_OK) return rc;
-        attr_set = true;
-    }
+    int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern), static_cast<int>(kMaxSmem),
+                                 "cudaFuncSetAttribute(stream decode)");
+    if (rc != QVP_OK) return rc;
+    rc = set_smem_limit_once(combine_attr_done, reinterpret_cast<const void*>(combine_records<D, HH, J>),
+                             kCombineWarps * 16 * D * static_cast<int>(sizeof(float)), "cudaFuncSetAttribute(combine)");
+    if (rc != QVP_OK) return rc;
     CUtensorMap map;
-    int rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
+    rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
     if (rc != QVP_OK) return rc;
     const uint32_t smem = S::kSmem + (sp.nseg + 1) * 4;
     {

@@ -397,16 +397,13 @@ __global__ void __launch_bounds__(kGenWarps * 32) paged_prefill_generic(const Pr
 template <int D, int NB, int STAGES>
 int launch_prefill_fast(const qvp_prefill_args& a, const PrefillParams& pp, cudaStream_t st) {
     using S = PrefillShape<D, NB, STAGES>;
-    static bool attr_set = false;
+    static std::atomic<std::uint64_t> attr_done{0};
     auto kern = paged_prefill_fast<D, NB, STAGES>;
-    if (!attr_set) {
-        const int rc = check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem),
-                                  "cudaFuncSetAttribute(prefill)");
-        if (rc != QVP_OK) return rc;
-        attr_set = true;
-    }
+    int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern), static_cast<int>(S::kSmem),
+                                 "cudaFuncSetAttribute(prefill)");
+    if (rc != QVP_OK) return rc;
     CUtensorMap map;
-    int rc = encode_pool_map(a.pool, a.num_blocks, a.shape, 1, &map);
+    rc = encode_pool_map(a.pool, a.num_blocks, a.shape, 1, &map);
     if (rc != QVP_OK) return rc;
     const dim3 grid(ceil_div(a.max_query_len, pp.tile_tokens), a.shape.num_kv_heads, a.batch);
     kern<<<grid, kPrefillThreads, S::kSmem, st>>>(map, pp);

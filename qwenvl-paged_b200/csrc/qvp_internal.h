@@ -6,6 +6,7 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstddef>
 #include <cstdint>
@@ -16,6 +17,12 @@ namespace qvp {
 int fail(int status, const char* fmt, ...);
 // Returns QVP_OK, or QVP_ERR_CUDA with `what` and the CUDA error text recorded.
 int check_cuda(cudaError_t err, const char* what);
+
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current
+// device. The attribute belongs to a device, so `done` (one per kernel)
+// records the devices already set (bit d for device d < 64; others are set
+// on every call).
+int set_smem_limit_once(std::atomic<std::uint64_t>& done, const void* func, int bytes, const char* what);
 
 inline bool is_pow2(uint32_t v) { return v != 0 && (v & (v - 1)) == 0; }
 inline size_t round_up(size_t v, size_t a) { return a == 0 ? v : (v + a - 1) / a * a; }
