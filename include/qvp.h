@@ -147,7 +147,8 @@ typedef struct qvp_decode_args {
     const void* query;             /* device [batch][num_query_heads][head_dim]*/
     void* out;                     /* device [batch][num_query_heads][head_dim]*/
     uint32_t split_tokens;         /* 0 = auto; fast path: a multiple of 16    */
-    void* workspace;               /* device scratch, >= qvp_decode_workspace_size */
+    void* workspace;               /* device scratch, >= qvp_decode_workspace_size,
+                                      16-byte aligned                              */
     size_t workspace_bytes;
     int32_t* error_word;           /* device int32 or NULL; never cleared here */
 } qvp_decode_args;

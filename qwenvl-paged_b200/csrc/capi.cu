@@ -3,6 +3,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <new>
 #include <string>
 
 namespace qvp {
@@ -98,7 +99,11 @@ extern "C" int qvp_pool_create(int device, const qvp_block_shape* shape, uint32_
         rc = check_cuda(cudaSetDevice(device), "cudaSetDevice");
         if (rc != QVP_OK) return rc;
     }
-    auto* pool = new qvp_pool;
+    auto* pool = new (std::nothrow) qvp_pool;
+    if (pool == nullptr) {
+        if (device >= 0 && device != prev) cudaSetDevice(prev);
+        return fail(QVP_ERR_NOMEM, "out of host memory");
+    }
     pool->device = device >= 0 ? device : prev;
     pool->shape = *shape;
     pool->stride = qvp_block_stride(shape);

@@ -1270,6 +1270,9 @@ extern "C" int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream) {
     if (plan.workspace_bytes > 0 && (a.workspace == nullptr || a.workspace_bytes < plan.workspace_bytes))
         return fail(QVP_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", plan.workspace_bytes,
                     a.workspace == nullptr ? size_t(0) : a.workspace_bytes);
+    // partial records are read back as float4
+    if (plan.workspace_bytes > 0 && (reinterpret_cast<uintptr_t>(a.workspace) & 15u) != 0)
+        return fail(QVP_ERR_WORKSPACE, "workspace is not 16-byte aligned");
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const size_t parts = static_cast<size_t>(a.batch) * plan.max_splits * a.num_query_heads;
     float* ws_o = static_cast<float*>(a.workspace);

@@ -93,6 +93,17 @@ def test_workspace_too_small_is_refused():
     assert qvp.decode(a) == qvp.ERR_WORKSPACE
 
 
+@pytest.mark.parametrize("split", [0, 256])  # stream-K records and split-K partials
+def test_misaligned_workspace_is_refused_before_any_launch(split):
+    a = _args(shape=qvp.make_shape(16, 1, 4, 128, 2), dtype=qvp.DTYPE_BF16, block_stride=32768,
+              num_query_heads=28, batch=2, max_blocks_per_seq=64, max_context_len=1024, split_tokens=split)
+    need = qvp.decode_plan(a)["workspace_bytes"]
+    assert need > 0
+    a.workspace, a.workspace_bytes = 0x10008, need + 64
+    assert qvp.decode(a) == qvp.ERR_WORKSPACE
+    assert "aligned" in qvp.last_error()
+
+
 def test_movers_reject_bad_arguments():
     lib = qvp.lib
     assert lib.qvp_copy_blocks(None, 256, 4, 256, None, 1, None, None) == qvp.ERR_INVALID
