@@ -178,8 +178,15 @@ void MemoryAllocator::flush_copies() {
         pairs_capacity_ = cap;
     }
     if (pairs_event_ == nullptr) {
-        cudaEvent_t ev;
-        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        cudaEvent_t ev = nullptr;
+        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            error_ = "could not create the copy-pair event";
+            pending_pairs_.clear();
+            pending_src_.clear();
+            pending_dst_.clear();
+            return;
+        }
         pairs_event_ = ev;
     } else {
         // the pinned list of the previous flush must have reached the device

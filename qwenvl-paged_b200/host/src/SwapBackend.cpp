@@ -171,12 +171,15 @@ bool DeviceSwapBackend::ensure_staging(std::size_t blocks) {
         cudaGetLastError();
         return false;
     }
-    staging_blocks_ = ids_capacity_ = want;
     if (ids_event_ == nullptr) {
-        cudaEvent_t ev;
-        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+        cudaEvent_t ev = nullptr;
+        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
         ids_event_ = ev;
     }
+    staging_blocks_ = ids_capacity_ = want;
     return true;
 }
 
