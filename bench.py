@@ -17,6 +17,12 @@ Multi-GPU (torchrun, one rank per GPU): cfg2 runs one independent batch per
 rank (different seeds, no collective on the data path, weak scaling); cfg4
 shards the kv heads of one batch across ranks (strong scaling).
 
+Other workloads (one JSON line each, one GPU): `cfg3` copy-on-write and
+`cfg5` swap churn through the C++ host layer; `engine`, cfg2-shaped decode
+steps through KVCacheManager + PagedDecodeBatch with per-step and resident
+block tables; `prefill`, causal prefill of 16 x 2048-token prompts
+(qvp_prefill, TFLOP/s).
+
 `--impl reference` times the reference's own CPU paged_attention_decode<T>
 (oracle/_ref, compiled from the reference sources; the C restatement when
 that library is absent) on the host cores, rank 0 only.
@@ -516,7 +522,12 @@ def run_scenario(args):
     import ctypes as C
     lib = C.CDLL(os.path.join(ROOT, "qwenvl-paged_b200", "lib", "libqvp_scenarios.so"))
     buf = C.create_string_buffer(1 << 16)
-    if args.workload == "cfg3":
+    if args.workload == "engine":
+        lib.qvp_scenario_engine.argtypes = [C.c_int] * 6 + [C.c_char_p, C.c_size_t]
+        rc = lib.qvp_scenario_engine(64, 512, 8192, max(args.steps, 1), args.warmup, 2, buf, len(buf))
+        metric, key, unit = ("cfg2-shaped decode step through KVCacheManager + PagedDecodeBatch (resident tables), "
+                             "algorithmic GB/s on wall time"), "resident_gbs", "GB/s"
+    elif args.workload == "cfg3":
         lib.qvp_scenario_cow.argtypes = [C.c_int] * 6 + [C.c_char_p, C.c_size_t]
         rc = lib.qvp_scenario_cow(16, 8, 2048, 64, 3, max(args.steps, 1), buf, len(buf))
         metric, key, unit = "copy-on-write materialisation, batched copy kernel GB/s (read+write)", "cow_gbs", "GB/s"
@@ -533,13 +544,180 @@ def run_scenario(args):
     print(json.dumps(line), flush=True)
 
 
+def prefill_flops(w, qlens) -> int:
+    """4*Hq*D per (query token, visible key): query token t of sequence b
+    sees keys [0, ctx_b - ql_b + t]."""
+    tot = 0
+    for c, ql in zip(w.context_lens.astype(np.int64), np.asarray(qlens, dtype=np.int64)):
+        tot += int(ql * (c - ql) + ql * (ql + 1) // 2)
+    return 4 * w.num_query_heads * w.head_dim * tot
+
+
+def measured_tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def run_prefill(args):
+    """Causal prefill (qvp_prefill) of Qwen2-VL-7B-shaped prompts: every
+    prompt token attends to the keys up to its own position, which the
+    reference computes as its decode at every position. One step = one
+    qvp_prefill over the whole batch; L2 is flushed before each timed launch
+    (the batch's K/V fit in L2)."""
+    import ctypes as C
+
+    import torch
+
+    import qvp
+
+    rank, world, local = dist_env()
+    if world > 1:
+        raise SystemExit("--workload prefill runs on one GPU")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B, L = args.prefill_batch, args.prompt
+    w = W.small(5, batch=B, ctx_lo=L, ctx_hi=L, hq=28, hkv=4, head_dim=128, dtype="bf16", pool_factor=1.25)
+    w.name = f"prefill-qwen2vl-7b-{B}x{L}"
+    ql = np.full(B, L, dtype=np.int32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    pool = torch.zeros(w.num_blocks * w.block_stride // 2, dtype=torch.bfloat16, device=dev)
+    pool.view(w.num_blocks, -1)[:, : w.block_bytes // 2].normal_(generator=g)
+    q = torch.randn(B, L, w.num_query_heads, w.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    tab = torch.from_numpy(w.tables).to(dev)
+    ctx = torch.from_numpy(w.context_lens).to(dev)
+    qld = torch.from_numpy(ql).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    a = qvp.PrefillArgs()
+    a.pool, a.block_stride, a.num_blocks = pool.data_ptr(), w.block_stride, w.num_blocks
+    a.shape = qvp.make_shape(16, 1, w.num_kv_heads, w.head_dim, 2)
+    a.dtype = qvp.DTYPE_BF16
+    a.layer, a.num_query_heads, a.scale, a.batch = 0, w.num_query_heads, w.scale, B
+    a.max_blocks_per_seq, a.max_query_len = w.pitch, L
+    a.block_tables, a.context_lens, a.query_lens = tab.data_ptr(), ctx.data_ptr(), qld.data_ptr()
+    a.query, a.out, a.error_word = q.data_ptr(), out.data_ptr(), err.data_ptr()
+    stream = torch.cuda.current_stream()
+
+    def step():
+        st = qvp.lib.qvp_prefill(C.byref(a), stream.cuda_stream)
+        if st != 0:
+            raise RuntimeError(f"qvp_prefill failed: {st} {qvp.last_error()}")
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in evs:
+        flush.zero_()
+        e0.record(stream)
+        step()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    sampler.stop()
+    if int(err.item()) != 0:
+        raise RuntimeError(f"prefill kernel reported device error bits {int(err.item())}")
+    ms = sum(e0.elapsed_time(e1) for e0, e1 in evs) / args.steps
+    flops = prefill_flops(w, ql)
+    tflops = flops / (ms * 1e-3) / 1e12
+    peak, peak_kind = measured_tensor_peak()
+
+    # e2e: queries up from pinned host memory, outputs back, inside the timed region
+    host_q = q.cpu().pin_memory()
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        q.copy_(host_q, non_blocking=True)
+        step()
+        host_out.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    cpu = None
+    if not args.no_cpu:
+        # the reference's prefill is its decode at each position: time it on a
+        # bounded sample of positions (the last ones of sequence 0, the most
+        # expensive), threads over positions
+        import oracle
+        host_pool = pool.view(torch.uint8).cpu().numpy().reshape(-1)
+        qb = host_q.view(torch.int16).numpy().view(np.uint16)
+        n = args.prefill_cpu_positions
+        seq = np.zeros(n, dtype=np.int64)
+        tok = np.arange(L - n, L, dtype=np.int64)
+        ctxs = (tok + 1).astype(np.int32)
+        sub = W.DecodeWorkload(w.name, 16, 1, w.num_kv_heads, w.head_dim, "bf16", w.num_query_heads, w.scale,
+                               ctxs, np.ascontiguousarray(w.tables[seq]), w.num_blocks, w.seed)
+        qq = np.ascontiguousarray(qb[seq, tok])
+        threads = cpu_threads()
+        kind = "reference" if oracle.ref_available() else "port"
+        if kind == "reference":
+            r = oracle.RefDecoder(sub, host_pool)
+            r.bind()
+            run = lambda: r.decode(qq, threads=threads)  # noqa: E731
+        else:
+            run = lambda: oracle.port_decode(sub, host_pool, qq, threads=threads)  # noqa: E731
+        t0 = time.perf_counter()
+        run()
+        dt = time.perf_counter() - t0
+        if kind == "reference":
+            r.close()
+        cflops = 4 * w.num_query_heads * w.head_dim * int(ctxs.astype(np.int64).sum())
+        cpu = {"value": round(cflops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": threads, "kind": kind,
+               "sample": f"per-position decode of the last {n} positions of sequence 0 ({cflops / 1e9:.1f} GFLOP)"}
+
+    line = {
+        "metric": "causal prefill attention TFLOP/s over the paged cache",
+        "value": round(tflops, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) K/V/Q, seeded scattered block tables",
+        "config": {"workload": w.name, "batch": B, "prompt_tokens": L, "heads": "28q/4kv", "head_dim": 128,
+                   "kernel": "paged_prefill_fast (TMA + mma.sync, causal per-row limits)",
+                   "l2": "flushed (256 MiB write) before each timed launch"},
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(tflops / peak, 4),
+                     "peak_source": f"{peak_kind} (MEASURED_PEAKS.json bf16_tflops)" if peak_kind == "measured"
+                     else "fallback 1.59 PFLOP/s", "traffic": None, "flops_per_step": flops},
+        "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": int(q.numel() * 2), "d2h_bytes_per_step": int(out.numel() * 2),
+                "path": "C ABI qvp_prefill; per step the queries H2D from pinned memory and the outputs D2H"},
+        "gpu_launches": args.steps,
+        "clocks": sampler.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
 def main():
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--workload", choices=["cfg2", "cfg1", "cfg4", "cfg3", "cfg5"], default="cfg2")
+    p.add_argument("--workload", choices=["cfg2", "cfg1", "cfg4", "cfg3", "cfg5", "prefill", "engine"],
+                   default="cfg2")
+    p.add_argument("--prompt", type=int, default=2048, help="prefill: prompt tokens per sequence")
+    p.add_argument("--prefill-batch", type=int, default=16, help="prefill: sequences")
+    p.add_argument("--prefill-cpu-positions", type=int, default=512,
+                   help="prefill: positions in the CPU baseline sample")
     p.add_argument("--swap-pool-blocks", type=int, default=1 << 20, help="cfg5 pool size in 64 KiB blocks")
     p.add_argument("--split", type=int, default=0, help="split-K partition in tokens (0 = auto)")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
@@ -554,7 +732,9 @@ def main():
     args = p.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload in ("cfg3", "cfg5") and args.impl == "ours":
+    if args.workload == "prefill" and args.impl == "ours":
+        run_prefill(args)
+    elif args.workload in ("cfg3", "cfg5", "engine") and args.impl == "ours":
         run_scenario(args)
     elif args.impl == "reference":
         run_reference(args)

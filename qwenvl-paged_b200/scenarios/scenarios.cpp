@@ -4,9 +4,11 @@
 //         block with one batched copy launch, decode all branches);
 //   cfg5  preemption / swap churn on a 1,048,576-block pool (swap out a
 //         seeded quarter of the resident sequences to pinned host memory,
-//         decode the rest, swap them back in).
+//         decode the rest, swap them back in);
+//   engine  cfg2-shaped decode steps through KVCacheManager and
+//         PagedDecodeBatch, with per-step and with resident block tables.
 // Each returns one JSON object of measurements. Loaded by bench.py
-// (--workload cfg3 / cfg5) from qwenvl-paged_b200/lib/libqvp_scenarios.so.
+// (--workload cfg3 / cfg5 / engine) from qwenvl-paged_b200/lib/libqvp_scenarios.so.
 #include "qwenvl_paged/KVCacheManager.h"
 #include "qwenvl_paged/MemoryAllocator.h"
 #include "qwenvl_paged/PagedAttention.h"
@@ -339,5 +341,160 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
        << ", \"resume_batch_decode_ms\": " << rdecode_ms << ", \"resume_batch_stall_ms\": " << stall_ms << ", \"resume_batch_sequences\": " << rviews.size()
        << ", \"pool_alloc_s\": " << pool_s << ", \"slab_pin_s\": " << pin_s << ", \"decode_ok\": "
        << (dec_ok ? "true" : "false") << ", \"decode_device_error\": " << derr << "}";
+    return emit(js.str(), out, cap);
+}
+
+// cfg2-shaped engine loop through the C++ API: `batch` sequences with seeded
+// contexts in [lo, hi]. A step gives every sequence one more token (reserve
+// at a block boundary, then ensure_token_writable) and decodes the batch with
+// PagedDecodeBatch. The loop runs twice, with the block tables flattened and
+// uploaded every step and with resident tables, each over `steps` timed steps
+// after `warmup`. Per mode it reports the wall time of a step (host
+// bookkeeping and decode, pipelined; the clock stops after the last decode
+// finishes), the host time inside the step calls, the device time (CUDA
+// events on the engine stream), GB/s on the decode's algorithmic bytes, and
+// the table rows and bytes uploaded. Both modes then decode the final state
+// once more and the outputs are compared byte for byte.
+extern "C" __attribute__((visibility("default"))) int qvp_scenario_engine(int batch, int lo, int hi, int steps,
+                                                                           int warmup, int seed, char* out,
+                                                                           size_t cap) {
+    const BlockShape sh = bf16_shape(4);
+    const std::uint32_t T = sh.tokens_per_block, hq = 28;
+    std::mt19937 rng(seed);
+    std::uniform_int_distribution<int> len(lo, hi);
+    std::vector<std::uint32_t> ctx(batch);
+    std::uint64_t need = 64;
+    const int grow = 2 * (steps + warmup) + 2;  // both modes advance every sequence
+    for (int b = 0; b < batch; ++b) {
+        ctx[b] = static_cast<std::uint32_t>(len(rng));
+        need += (ctx[b] + grow + T - 1) / T + 1;
+    }
+    AllocatorConfig cfg;
+    cfg.block_shape = sh;
+    cfg.max_blocks = static_cast<std::uint32_t>(need + need / 10);
+    MemoryAllocator alloc(cfg);
+    if (!alloc.has_storage()) return emit("{\"error\": \"pool allocation failed\"}", out, cap);
+    KVCacheManager cache(alloc);
+    std::vector<SequenceId> seqs;
+    for (int b = 0; b < batch; ++b) {
+        const SequenceId s = static_cast<SequenceId>(b + 1);
+        if (!cache.create_sequence(SequenceMetadata{s, s, {}, {}}) || !cache.reserve_tokens(s, ctx[b]))
+            return emit("{\"error\": \"could not reserve the contexts\"}", out, cap);
+        seqs.push_back(s);
+    }
+    // seeded bf16 values over the whole pool, 64 blocks per copy
+    {
+        const std::size_t stride = alloc.block_stride(), chunk = 64;
+        std::vector<bfloat16> h(2 * chunk * stride / 2);  // chunks start at rotating offsets
+        std::normal_distribution<float> nd;
+        for (auto& x : h) x = bfloat16(nd(rng));
+        auto* base = reinterpret_cast<std::uint8_t*>(alloc.pool_base());
+        for (std::size_t b0 = 0; b0 < cfg.max_blocks; b0 += chunk) {
+            const std::size_t n = std::min<std::size_t>(chunk, cfg.max_blocks - b0);
+            const std::size_t rot = (b0 / chunk * 4099) % (h.size() - n * stride / 2 + 1);
+            cudaMemcpy(base + b0 * stride, h.data() + rot, n * stride, cudaMemcpyHostToDevice);
+        }
+    }
+    const std::size_t qel = static_cast<std::size_t>(batch) * hq * sh.head_dim;
+    void* q = device_query(qel, seed + 1);
+    void *o1 = nullptr, *o2 = nullptr;
+    cudaMalloc(&o1, qel * 2);
+    cudaMalloc(&o2, qel * 2);
+    const float scale = 1.f / std::sqrt(128.f);
+    bool ok = true;
+
+    auto advance = [&]() {
+        for (int b = 0; b < batch; ++b) {
+            if (ctx[b] % T == 0) ok = cache.reserve_tokens(seqs[b], 1) && ok;
+            ok = cache.ensure_token_writable(seqs[b], ctx[b]).has_value() && ok;
+            ++ctx[b];
+        }
+    };
+    auto views = [&]() {
+        std::vector<CacheView> v;
+        v.reserve(seqs.size());
+        for (SequenceId s : seqs) v.push_back(*cache.cache_view(s));
+        return v;
+    };
+    auto alg_bytes = [&]() {
+        double kv = 0, tbl = 0;
+        for (std::uint32_t c : ctx) {
+            kv += 2.0 * c * sh.num_kv_heads * sh.head_dim * 2;
+            tbl += 4.0 * ((c + T - 1) / T);
+        }
+        return kv + tbl + 2.0 * qel * 2;
+    };
+
+    struct Result {
+        double wall_us, host_us, device_us, gbs, device_gbs, rows, upload_bytes;
+        int status, device_error;
+    };
+    PagedDecodeBatch flat(alloc), resident(alloc, true);
+    auto run_mode = [&](PagedDecodeBatch& pb, void* o) {
+        Result r{};
+        for (int i = 0; i < warmup; ++i) {
+            advance();
+            ok = pb.run(views(), ctx, 0, hq, scale, q, o) && ok;
+        }
+        cudaStreamSynchronize(alloc.stream());
+        Events ev;
+        double host = 0, alg = 0, rows = 0, bytes = 0;
+        const double t0 = now_s();
+        cudaEventRecord(ev.a, alloc.stream());
+        for (int i = 0; i < steps; ++i) {
+            const double th = now_s();
+            advance();
+            ok = pb.run(views(), ctx, 0, hq, scale, q, o) && ok;
+            host += now_s() - th;
+            alg += alg_bytes();
+            rows += pb.rows_uploaded();
+            bytes += static_cast<double>(pb.bytes_uploaded());
+        }
+        cudaEventRecord(ev.b, alloc.stream());
+        cudaStreamSynchronize(alloc.stream());
+        const double wall = now_s() - t0;
+        const double dev_s = ev.ms() * 1e-3;
+        const int n = std::max(steps, 1);
+        r.wall_us = wall / n * 1e6;
+        r.host_us = host / n * 1e6;
+        r.device_us = dev_s / n * 1e6;
+        r.gbs = alg / wall / 1e9;
+        r.device_gbs = alg / dev_s / 1e9;
+        r.rows = rows / n;
+        r.upload_bytes = bytes / n;
+        r.status = pb.last_status();
+        r.device_error = pb.device_error();
+        return r;
+    };
+    const Result rf = run_mode(flat, o1);
+    const Result rr = run_mode(resident, o2);
+    // the same final state through both modes
+    const std::vector<CacheView> fin = views();
+    ok = flat.run(fin, ctx, 0, hq, scale, q, o1) && ok;
+    ok = resident.run(fin, ctx, 0, hq, scale, q, o2) && ok;
+    cudaStreamSynchronize(alloc.stream());
+    std::vector<std::uint8_t> a(qel * 2), b(qel * 2);
+    cudaMemcpy(a.data(), o1, a.size(), cudaMemcpyDeviceToHost);
+    cudaMemcpy(b.data(), o2, b.size(), cudaMemcpyDeviceToHost);
+    const bool same = std::memcmp(a.data(), b.data(), a.size()) == 0;
+    cudaFree(q);
+    cudaFree(o1);
+    cudaFree(o2);
+
+    std::ostringstream js;
+    auto mode = [&](const char* name, const Result& r) {
+        js << "\"" << name << "\": {\"wall_us_per_step\": " << r.wall_us << ", \"host_us_per_step\": " << r.host_us
+           << ", \"device_us_per_step\": " << r.device_us << ", \"gbs\": " << r.gbs
+           << ", \"device_gbs\": " << r.device_gbs << ", \"rows_uploaded_per_step\": " << r.rows
+           << ", \"upload_bytes_per_step\": " << r.upload_bytes << ", \"status\": " << r.status
+           << ", \"device_error\": " << r.device_error << "}";
+    };
+    js << "{\"workload\": \"engine-cfg2-qwen2vl-7b-decode\", \"batch\": " << batch << ", \"ctx_range\": [" << lo
+       << ", " << hi << "], \"steps\": " << steps << ", \"warmup\": " << warmup << ", ";
+    mode("flattened_tables", rf);
+    js << ", ";
+    mode("resident_tables", rr);
+    js << ", \"resident_gbs\": " << rr.gbs << ", \"outputs_identical\": " << (same ? "true" : "false")
+       << ", \"all_ok\": " << (ok ? "true" : "false") << "}";
     return emit(js.str(), out, cap);
 }

@@ -95,3 +95,12 @@ def test_prefill_rejects_inconsistent_arguments_before_any_launch(bad):
 def test_prefill_with_an_empty_batch_is_a_no_op():
     import ctypes as C
     assert qvp.lib.qvp_prefill(C.byref(_args(batch=0)), None) == qvp.OK
+
+
+def test_bench_prefill_flops_count_every_visible_key():
+    import bench
+    w = W.small(3, batch=3, ctx_lo=5, ctx_hi=60, hq=8, hkv=2, head_dim=16, dtype="bf16")
+    ql = np.array([1, 4, min(17, int(w.context_lens[2]))], dtype=np.int32)
+    ql = np.minimum(ql, w.context_lens)
+    _, _, ctx = oracle.prefill_pairs(w, ql)
+    assert bench.prefill_flops(w, ql) == 4 * w.num_query_heads * w.head_dim * int(ctx.astype(np.int64).sum())
