@@ -4,11 +4,14 @@
 // `writable`. `entries()` order is what a batch step flattens into the device
 // int32 tables.
 //
-// Beyond the reference interface, revision() stamps the table's contents: a
-// process-wide counter value taken at construction and at every call that can
+// Beyond the reference interface, revision() stamps the table's contents as
+// {instance, count}: {0, 0} for a table with no entries (new or moved from);
+// otherwise `instance` is a process-unique id the table takes at its first
+// change (or when it is copied) and `count` advances at every call that can
 // change a mapping (map, unmap, set_writable, mutable_entry, fork). Two table
 // states with the same stamp hold the same entries, so a device-resident copy
-// of the table can be refreshed only when the stamp moves.
+// of the table can be refreshed only when the stamp moves. A change costs one
+// increment; only a table's first change takes the shared id counter.
 #pragma once
 
 #include "qwenvl_paged/Block.h"
@@ -19,6 +22,15 @@
 #include <vector>
 
 namespace qwenvl_paged {
+
+struct TableStamp {
+    std::uint64_t instance{0};
+    std::uint64_t count{0};
+    friend bool operator==(const TableStamp& a, const TableStamp& b) noexcept {
+        return a.instance == b.instance && a.count == b.count;
+    }
+    friend bool operator!=(const TableStamp& a, const TableStamp& b) noexcept { return !(a == b); }
+};
 
 struct BlockTableEntry {
     LogicalBlock logical{};
@@ -32,8 +44,8 @@ struct BlockTableEntry {
 class BlockTable {
 public:
     explicit BlockTable(SequenceId sequence_id, CacheKind cache_kind = CacheKind::TextKV);
-    BlockTable(const BlockTable&) = default;
-    BlockTable& operator=(const BlockTable&) = default;
+    BlockTable(const BlockTable& other);
+    BlockTable& operator=(const BlockTable& other);
     BlockTable(BlockTable&& other) noexcept;
     BlockTable& operator=(BlockTable&& other) noexcept;
 
@@ -50,7 +62,7 @@ public:
     void set_writable(LogicalBlockIndex index, bool writable);
     [[nodiscard]] const std::vector<BlockTableEntry>& entries() const noexcept;
     [[nodiscard]] BlockTable fork(SequenceId child_sequence_id) const;
-    [[nodiscard]] std::uint64_t revision() const noexcept;
+    [[nodiscard]] TableStamp revision() const noexcept;
 
 private:
     // Position of the first entry whose logical index is >= `index`.
@@ -58,8 +70,10 @@ private:
 
     SequenceId sequence_id_{0};
     CacheKind cache_kind_{CacheKind::TextKV};
+    void touch() noexcept;
+
     std::vector<BlockTableEntry> entries_;
-    std::uint64_t revision_{0};
+    TableStamp stamp_{};
 };
 
 }  // namespace qwenvl_paged

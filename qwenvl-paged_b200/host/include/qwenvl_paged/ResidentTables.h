@@ -65,7 +65,7 @@ public:
 private:
     struct Row {
         const BlockTable* table{nullptr};
-        std::uint64_t revision{0};
+        TableStamp revision{};
         std::uint32_t valid{0};  // leading entries that resolve to a pool block
     };
     void write_row(std::uint32_t b, const BlockTable& table);

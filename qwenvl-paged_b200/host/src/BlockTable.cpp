@@ -6,23 +6,40 @@
 namespace qwenvl_paged {
 
 namespace {
-std::uint64_t next_revision() noexcept {
+std::uint64_t next_instance() noexcept {
     static std::atomic<std::uint64_t> counter{0};
     return counter.fetch_add(1, std::memory_order_relaxed) + 1;
 }
 }  // namespace
 
 BlockTable::BlockTable(SequenceId sequence_id, CacheKind cache_kind)
-    : sequence_id_(sequence_id), cache_kind_(cache_kind), revision_(next_revision()) {}
+    : sequence_id_(sequence_id), cache_kind_(cache_kind) {}
 
-// A moved-from table is left empty under a fresh stamp.
+// A copy holds the same entries under an id of its own, so that the two
+// tables can change independently without ever sharing a stamp.
+BlockTable::BlockTable(const BlockTable& other)
+    : sequence_id_(other.sequence_id_), cache_kind_(other.cache_kind_), entries_(other.entries_) {
+    if (!entries_.empty()) stamp_ = TableStamp{next_instance(), 1};
+}
+
+BlockTable& BlockTable::operator=(const BlockTable& other) {
+    if (this != &other) {
+        sequence_id_ = other.sequence_id_;
+        cache_kind_ = other.cache_kind_;
+        entries_ = other.entries_;
+        stamp_ = entries_.empty() ? TableStamp{} : TableStamp{next_instance(), 1};
+    }
+    return *this;
+}
+
+// A moved-from table is left empty, under the stamp of an empty table.
 BlockTable::BlockTable(BlockTable&& other) noexcept
     : sequence_id_(other.sequence_id_),
       cache_kind_(other.cache_kind_),
       entries_(std::move(other.entries_)),
-      revision_(other.revision_) {
+      stamp_(other.stamp_) {
     other.entries_.clear();
-    other.revision_ = next_revision();
+    other.stamp_ = TableStamp{};
 }
 
 BlockTable& BlockTable::operator=(BlockTable&& other) noexcept {
@@ -30,14 +47,19 @@ BlockTable& BlockTable::operator=(BlockTable&& other) noexcept {
         sequence_id_ = other.sequence_id_;
         cache_kind_ = other.cache_kind_;
         entries_ = std::move(other.entries_);
-        revision_ = other.revision_;
+        stamp_ = other.stamp_;
         other.entries_.clear();
-        other.revision_ = next_revision();
+        other.stamp_ = TableStamp{};
     }
     return *this;
 }
 
-std::uint64_t BlockTable::revision() const noexcept { return revision_; }
+void BlockTable::touch() noexcept {
+    if (stamp_.instance == 0) stamp_.instance = next_instance();
+    ++stamp_.count;
+}
+
+TableStamp BlockTable::revision() const noexcept { return stamp_; }
 
 std::size_t BlockTable::position(LogicalBlockIndex index) const noexcept {
     std::size_t lo = 0, hi = entries_.size();
@@ -57,7 +79,7 @@ std::size_t BlockTable::size() const noexcept { return entries_.size(); }
 bool BlockTable::empty() const noexcept { return entries_.empty(); }
 
 void BlockTable::map(LogicalBlock logical, PhysicalBlockId physical_id, bool writable) {
-    revision_ = next_revision();
+    touch();
     const std::size_t at = position(logical.index);
     if (at < entries_.size() && entries_[at].logical.index == logical.index) {
         BlockTableEntry& e = entries_[at];
@@ -77,7 +99,7 @@ void BlockTable::map(LogicalBlock logical, PhysicalBlockId physical_id, bool wri
 std::optional<PhysicalBlockId> BlockTable::unmap(LogicalBlockIndex index) {
     const std::size_t at = position(index);
     if (at == entries_.size() || entries_[at].logical.index != index) return std::nullopt;
-    revision_ = next_revision();
+    touch();
     const PhysicalBlockId id = entries_[at].physical_id;
     entries_.erase(entries_.begin() + static_cast<std::ptrdiff_t>(at));
     return id;
@@ -96,7 +118,7 @@ const BlockTableEntry* BlockTable::entry(LogicalBlockIndex index) const noexcept
 
 // The caller may change the entry through the pointer, so the stamp moves.
 BlockTableEntry* BlockTable::mutable_entry(LogicalBlockIndex index) noexcept {
-    revision_ = next_revision();
+    touch();
     return const_cast<BlockTableEntry*>(static_cast<const BlockTable*>(this)->entry(index));
 }
 
@@ -109,7 +131,7 @@ const std::vector<BlockTableEntry>& BlockTable::entries() const noexcept { retur
 BlockTable BlockTable::fork(SequenceId child_sequence_id) const {
     BlockTable child = *this;
     child.sequence_id_ = child_sequence_id;
-    child.revision_ = next_revision();
+    child.touch();
     for (BlockTableEntry& e : child.entries_) {
         e.writable = false;
         e.logical.sequence_id = child_sequence_id;
