@@ -49,6 +49,21 @@ struct HostMemoryOptions {
     bool prefer_pinned_memory{false};
 };
 
+// Host-visible block storage (not part of the reference interface). By
+// default block bytes live in device memory, and PhysicalBlock::data() and
+// CacheView::slot<T>() are device addresses. With host-visible storage, pools
+// and standalone blocks are CUDA managed memory: the same addresses can also
+// be read and written from the host, as in the reference, at the cost of page
+// migration. Decode over such a pool never uses the TMA view of the pool
+// (the pool's block stride is padded), and copy-on-write copies complete
+// before MemoryAllocator::copy_block returns. This mode is meant for code
+// that touches block bytes from the host, such as the reference's tests; it
+// is not for serving. Off unless QVP_HOST_VISIBLE_POOLS=1 is set in the
+// environment; set_host_visible_pools() changes it for allocations made
+// afterwards.
+[[nodiscard]] bool host_visible_pools() noexcept;
+void set_host_visible_pools(bool on) noexcept;
+
 struct LogicalBlock {
     SequenceId sequence_id{0};
     LogicalBlockIndex index{0};
@@ -62,7 +77,8 @@ struct LogicalBlock {
 // Bytes of one physical block in device memory.
 //
 // A block built with the public constructor owns its own device allocation
-// (one cudaMalloc, released by the destructor). Blocks handed out by a
+// (one cudaMalloc, or cudaMallocManaged with host-visible storage, released
+// by the destructor). Blocks handed out by a
 // MemoryAllocator are views into the allocator's pool and own nothing.
 class PhysicalBlock {
 public:

@@ -38,6 +38,7 @@ struct DevicePoolOptions {
     int device{-1};                  // CUDA ordinal; -1 = the current device
     bool allocate_storage{true};     // false: bookkeeping only, no device bytes
     CUstream_st* stream{nullptr};    // engine stream for copies and swaps (null = legacy default)
+    bool host_visible{host_visible_pools()};  // managed memory; see host_visible_pools()
 };
 
 struct AllocatorStats {
@@ -99,6 +100,7 @@ public:
     bool write_bytes(PhysicalBlockId id, std::size_t offset, const void* host, std::size_t bytes);
     bool read_bytes(PhysicalBlockId id, std::size_t offset, void* host, std::size_t bytes);
     [[nodiscard]] bool has_storage() const noexcept { return pool_ != nullptr; }
+    [[nodiscard]] bool host_visible() const noexcept { return host_visible_; }
     [[nodiscard]] std::byte* pool_base() const noexcept { return pool_; }
     [[nodiscard]] std::size_t block_stride() const noexcept { return stride_; }
     [[nodiscard]] std::uint32_t num_blocks() const noexcept { return config_.max_blocks; }
@@ -119,6 +121,7 @@ private:
     AllocatorConfig config_{};
     int device_{-1};
     CUstream_st* stream_{nullptr};
+    bool host_visible_{false};
     std::byte* pool_{nullptr};
     std::size_t stride_{0};
     std::vector<std::unique_ptr<PhysicalBlock>> blocks_;

@@ -1,5 +1,8 @@
 #include "qwenvl_paged/Block.h"
 
+#include <atomic>
+#include <cstdlib>
+
 #include <cuda_runtime.h>
 
 namespace qwenvl_paged {
@@ -20,13 +23,28 @@ std::size_t BlockShape::byte_size() const noexcept {
 
 bool LogicalBlock::empty() const noexcept { return token_count == 0; }
 
+namespace {
+std::atomic<int>& host_visible_flag() {
+    static std::atomic<int> flag{[] {
+        const char* v = std::getenv("QVP_HOST_VISIBLE_POOLS");
+        return (v != nullptr && v[0] == '1') ? 1 : 0;
+    }()};
+    return flag;
+}
+}  // namespace
+
+bool host_visible_pools() noexcept { return host_visible_flag().load(std::memory_order_relaxed) != 0; }
+void set_host_visible_pools(bool on) noexcept { host_visible_flag().store(on ? 1 : 0, std::memory_order_relaxed); }
+
 PhysicalBlock::PhysicalBlock(PhysicalBlockId id, BlockShape shape, HostMemoryOptions memory_options)
     : id_(id), shape_(shape), memory_options_(memory_options) {
     size_bytes_ = rounded(shape_.byte_size(), memory_options_.alignment_bytes);
     void* p = nullptr;
-    // cudaMalloc returns addresses aligned to at least 256 bytes, the
-    // reference's default block alignment.
-    if (cudaMalloc(&p, size_bytes_) == cudaSuccess) {
+    // cudaMalloc and cudaMallocManaged return addresses aligned to at least
+    // 256 bytes, the reference's default block alignment.
+    const cudaError_t e = host_visible_pools() ? cudaMallocManaged(&p, size_bytes_, cudaMemAttachGlobal)
+                                               : cudaMalloc(&p, size_bytes_);
+    if (e == cudaSuccess) {
         storage_ = static_cast<std::byte*>(p);
         owns_storage_ = true;
     } else {

@@ -33,19 +33,21 @@ struct DeviceGuard {
 MemoryAllocator::MemoryAllocator(AllocatorConfig config) : MemoryAllocator(config, DevicePoolOptions{}) {}
 
 MemoryAllocator::MemoryAllocator(AllocatorConfig config, DevicePoolOptions options)
-    : config_(config), device_(options.device), stream_(options.stream) {
+    : config_(config), device_(options.device), stream_(options.stream), host_visible_(options.host_visible) {
     const std::size_t alignment =
         config_.memory_options.alignment_bytes == 0 ? kDefaultBlockAlignmentBytes : config_.memory_options.alignment_bytes;
     std::size_t block_size = round_to(config_.block_shape.byte_size(), alignment);
     if (block_size == 0) block_size = alignment;
     stride_ = round_to(block_size, 256);
+    // a padded stride keeps decode over managed memory off the TMA view
+    if (host_visible_) stride_ += round_to(256, alignment);
 
     if (options.allocate_storage && config_.max_blocks > 0) {
         DeviceGuard guard(device_);
         if (device_ < 0) cudaGetDevice(&device_);
         void* p = nullptr;
         const std::size_t total = stride_ * config_.max_blocks;
-        const cudaError_t e = cudaMalloc(&p, total);
+        const cudaError_t e = host_visible_ ? cudaMallocManaged(&p, total, cudaMemAttachGlobal) : cudaMalloc(&p, total);
         if (e == cudaSuccess) {
             pool_ = static_cast<std::byte*>(p);
             cudaMemset(pool_, 0, total);
@@ -92,6 +94,7 @@ MemoryAllocator& MemoryAllocator::operator=(MemoryAllocator&& o) noexcept {
     config_ = o.config_;
     device_ = o.device_;
     stream_ = o.stream_;
+    host_visible_ = o.host_visible_;
     pool_ = std::exchange(o.pool_, nullptr);
     stride_ = o.stride_;
     blocks_ = std::move(o.blocks_);
@@ -152,6 +155,12 @@ void MemoryAllocator::copy_block(PhysicalBlockId source, PhysicalBlockId destina
     pending_pairs_.push_back(static_cast<std::int32_t>(destination));
     pending_src_.insert(source);
     pending_dst_.insert(destination);
+    if (host_visible_) {
+        // host code may read or write either block next: the copy lands now
+        flush_copies();
+        DeviceGuard guard(device_);
+        if (cudaStreamSynchronize(stream_) != cudaSuccess) error_ = cudaGetErrorString(cudaGetLastError());
+    }
 }
 
 void MemoryAllocator::flush_copies() {

@@ -1,6 +1,8 @@
-// TEST INFRASTRUCTURE: host checks of the resident block tables
-// (qwenvl_paged/ResidentTables.h). Each packet the planner emits is applied to
-// a host mirror of the device table, the way qvp_scatter_blocks and the copy
+// TEST INFRASTRUCTURE: host checks of this library's additions to the
+// reference interface: the resident block tables (qwenvl_paged/
+// ResidentTables.h) and host-visible pools (qwenvl_paged/Block.h). For the
+// tables, each packet the planner emits is applied to a host mirror of the
+// device table, the way qvp_scatter_blocks and the copy
 // of the context lengths apply it on the device, and after every step the
 // mirror must hold, for every sequence, the same ids over its context as a
 // full per-step flatten of its BlockTable. Bookkeeping-only pools, so all of
@@ -291,6 +293,24 @@ NATIVE_TEST(random_engine_scripts_match_the_full_flatten_every_step) {
             (void)step(p, m, v, ctx, 512);
         }
     }
+}
+
+// ---- host-visible pools (the other addition to the reference interface) ----
+
+NATIVE_TEST(host_visible_pools_pad_the_stride_and_follow_the_process_setting) {
+    const bool before = host_visible_pools();
+    set_host_visible_pools(false);
+    CHECK(!DevicePoolOptions{}.host_visible);
+    MemoryAllocator plain(config(8), DevicePoolOptions{-1, false, nullptr});
+    set_host_visible_pools(true);
+    CHECK(DevicePoolOptions{}.host_visible);
+    MemoryAllocator visible(config(8), DevicePoolOptions{-1, false, nullptr});
+    set_host_visible_pools(before);
+    CHECK(!plain.host_visible() && visible.host_visible());
+    // the padded stride keeps decode off the TMA view of a managed pool
+    CHECK(plain.block_stride() == config(8).block_shape.byte_size());
+    CHECK(visible.block_stride() > config(8).block_shape.byte_size() && visible.block_stride() % 256 == 0);
+    CHECK(visible.block(1)->size_bytes() == plain.block(1)->size_bytes());
 }
 
 }  // namespace
