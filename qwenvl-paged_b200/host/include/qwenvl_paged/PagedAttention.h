@@ -118,4 +118,76 @@ private:
     std::string error_;
 };
 
+// Causal prefill of one layer for a batch (no reference counterpart: the
+// reference computes prefill as its decode at every prompt position,
+// include/qwenvl_paged/PagedAttention.h:43-44; this runs qvp_prefill, which
+// gives the same values). For sequence b, the last query_lens[b] of its
+// context_lens[b] cached tokens are queries: each attends to every key up to
+// its own position. Their K and V must already be in the cache
+// (KVAppendBatch, or host writes into a host-visible pool). `query` and
+// `out` are device arrays [batch][max(query_lens)][num_query_heads]
+// [head_dim] in the pool's element type. The checks and the refusal rules
+// are PagedDecodeBatch's, plus query_lens[b] in [1, context_lens[b]].
+class PagedPrefillBatch {
+public:
+    explicit PagedPrefillBatch(const MemoryAllocator& allocator);
+    ~PagedPrefillBatch();
+    PagedPrefillBatch(const PagedPrefillBatch&) = delete;
+    PagedPrefillBatch& operator=(const PagedPrefillBatch&) = delete;
+
+    bool run(const std::vector<CacheView>& views, const std::vector<std::uint32_t>& context_lens,
+             const std::vector<std::uint32_t>& query_lens, std::uint32_t layer, std::uint32_t num_query_heads,
+             float scale, const void* query, void* out);
+
+    [[nodiscard]] int last_status() const noexcept { return status_; }
+    [[nodiscard]] const std::string& last_error() const noexcept { return error_; }
+    // Device error bits of the last run (qvp_prefill error word); waits for it.
+    [[nodiscard]] int device_error();
+
+private:
+    const MemoryAllocator* allocator_;
+    std::int32_t* host_buf_{nullptr};  // pinned: tables, context lengths, query lengths
+    std::int32_t* dev_buf_{nullptr};
+    std::size_t buf_ints_{0};
+    std::int32_t* error_word_{nullptr};
+    void* upload_event_{nullptr};
+    int status_{0};
+    std::string error_;
+};
+
+// Writes one new token's K and V per sequence (no reference counterpart: the
+// reference's tests store them through CacheView::slot<T>() after
+// KVCacheManager::ensure_token_writable, tests/PagedAttention.test.cpp:
+// 97-127). Token positions[b] of views[b] goes to slot positions[b] %
+// tokens_per_block of its block, for layer `layer`. The block must be mapped,
+// writable and held by this sequence alone (call ensure_token_writable
+// first), otherwise nothing is written and run() returns false. `k` and `v`
+// are device arrays [batch][num_kv_heads][head_dim] in the pool's element
+// type. Enqueued on the allocator's stream after any queued copy-on-write
+// copies, one launch per call.
+class KVAppendBatch {
+public:
+    explicit KVAppendBatch(const MemoryAllocator& allocator);
+    ~KVAppendBatch();
+    KVAppendBatch(const KVAppendBatch&) = delete;
+    KVAppendBatch& operator=(const KVAppendBatch&) = delete;
+
+    bool run(const std::vector<CacheView>& views, const std::vector<std::uint32_t>& positions, std::uint32_t layer,
+             const void* k, const void* v);
+
+    [[nodiscard]] int last_status() const noexcept { return status_; }
+    [[nodiscard]] const std::string& last_error() const noexcept { return error_; }
+    [[nodiscard]] int device_error();
+
+private:
+    const MemoryAllocator* allocator_;
+    std::int32_t* host_buf_{nullptr};  // pinned: tables, positions
+    std::int32_t* dev_buf_{nullptr};
+    std::size_t buf_ints_{0};
+    std::int32_t* error_word_{nullptr};
+    void* upload_event_{nullptr};
+    int status_{0};
+    std::string error_;
+};
+
 }  // namespace qwenvl_paged

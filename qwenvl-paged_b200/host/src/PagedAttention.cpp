@@ -1,6 +1,7 @@
 #include "qwenvl_paged/PagedAttention.h"
 
 #include "qvp.h"
+#include "host_impl.h"
 
 #include <cuda_runtime.h>
 
@@ -10,92 +11,7 @@ namespace qwenvl_paged {
 
 namespace {
 
-struct OnDevice {
-    int prev = -1;
-    bool switched = false;
-    explicit OnDevice(int device) {
-        if (device >= 0 && cudaGetDevice(&prev) == cudaSuccess && prev != device &&
-            cudaSetDevice(device) == cudaSuccess)
-            switched = true;
-        cudaGetLastError();
-    }
-    ~OnDevice() {
-        if (switched) cudaSetDevice(prev);
-    }
-};
-
-bool is_device_pointer(const void* p) {
-    cudaPointerAttributes a{};
-    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
-    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
-}
-
-// The host-side checks of the reference kernel (PagedAttention.h:59-89):
-// shape/argument consistency, then every block of [0, context_len) must be
-// resolvable. Appends the physical ids of those blocks to `ids`.
-bool resolve(const CacheView& view, std::size_t elem_bytes, std::uint32_t layer, std::uint32_t num_query_heads,
-             std::uint32_t context_len, std::vector<std::int32_t>& ids) {
-    if (!view.valid()) return false;
-    const BlockShape& sh = view.layout.shape;
-    if (elem_bytes != sh.bytes_per_element || context_len == 0 || layer >= sh.num_layers ||
-        num_query_heads == 0 || num_query_heads % sh.num_kv_heads != 0)
-        return false;
-    const std::uint32_t tpb = sh.tokens_per_block;
-    const std::uint32_t nblk = (context_len + tpb - 1) / tpb;
-    for (std::uint32_t i = 0; i < nblk; ++i) {
-        const std::optional<PhysicalBlockId> id = view.block_table->lookup(i);
-        if (!id || view.allocator->block(*id) == nullptr) return false;
-        ids.push_back(static_cast<std::int32_t>(*id));
-    }
-    return true;
-}
-
-// The arguments part of resolve(), without walking the table.
-bool arguments_fit(const CacheView& view, std::size_t elem_bytes, std::uint32_t layer, std::uint32_t num_query_heads,
-                   std::uint32_t context_len) {
-    if (!view.valid()) return false;
-    const BlockShape& sh = view.layout.shape;
-    return elem_bytes == sh.bytes_per_element && context_len != 0 && layer < sh.num_layers && num_query_heads != 0 &&
-           num_query_heads % sh.num_kv_heads == 0;
-}
-
-// Writes the physical ids of blocks [0, nblk) into `row` by one pass over the
-// table's sorted entries; false if any of them is unmapped or swapped (the
-// same blocks resolve() would refuse).
-bool write_row(const CacheView& view, std::uint32_t nblk, std::int32_t* row) {
-    const std::vector<BlockTableEntry>& es = view.block_table->entries();
-    const std::uint32_t limit = view.allocator->num_blocks();
-    if (es.size() < nblk) return false;
-    for (std::uint32_t i = 0; i < nblk; ++i) {
-        const BlockTableEntry& e = es[i];
-        // sorted and unique: entry i maps logical block i iff its index is i
-        if (e.logical.index != i || e.swap_slot.has_value() || e.physical_id >= limit) return false;
-        row[i] = static_cast<std::int32_t>(e.physical_id);
-    }
-    return true;
-}
-
-int dtype_for(std::size_t elem_bytes) {
-    return elem_bytes == 4 ? QVP_DTYPE_F32 : elem_bytes == 2 ? QVP_DTYPE_BF16 : -1;
-}
-
-qvp_decode_args base_args(const MemoryAllocator& alloc, std::size_t elem_bytes, std::uint32_t layer,
-                          std::uint32_t num_query_heads, float scale) {
-    qvp_decode_args a{};
-    const BlockShape& sh = alloc.block_shape();
-    a.pool = alloc.pool_base();
-    a.block_stride = alloc.block_stride();
-    a.num_blocks = alloc.num_blocks();
-    a.shape = {sh.tokens_per_block, sh.num_layers, sh.num_kv_heads, sh.head_dim, sh.bytes_per_element};
-    a.dtype = dtype_for(elem_bytes);
-    a.layer = layer;
-    a.num_query_heads = num_query_heads;
-    a.scale = scale;
-    return a;
-}
+using namespace host_impl;
 
 // Device scratch of the single-sequence shim, grown on demand.
 struct ShimBuffers {

@@ -1,6 +1,7 @@
 #include "qwenvl_paged/ResidentTables.h"
 
 #include "qvp.h"
+#include "host_impl.h"
 
 #include <cuda_runtime.h>
 
@@ -13,19 +14,7 @@ namespace {
 
 std::size_t round4(std::size_t n) { return (n + 3) / 4 * 4; }
 
-struct OnDevice {
-    int prev = -1;
-    bool switched = false;
-    explicit OnDevice(int device) {
-        if (device >= 0 && cudaGetDevice(&prev) == cudaSuccess && prev != device &&
-            cudaSetDevice(device) == cudaSuccess)
-            switched = true;
-        cudaGetLastError();
-    }
-    ~OnDevice() {
-        if (switched) cudaSetDevice(prev);
-    }
-};
+using host_impl::OnDevice;
 
 }  // namespace
 

@@ -1,8 +1,11 @@
-// TEST INFRASTRUCTURE: GPU checks of PagedDecodeBatch with device-resident
-// block tables against the per-step flatten, on one device pool: over decode
-// steps that cross block boundaries, copy on write, reorder the batch and
-// refuse a swapped-out sequence, both must write bit-identical outputs.
-// Driven by tests/resident_tables_gpu_checks.py.
+// TEST INFRASTRUCTURE: GPU checks of the host layer's additions on device
+// pools, driven by tests/host_layer_gpu_checks.py:
+//  * PagedDecodeBatch with device-resident block tables against the per-step
+//    flatten: over decode steps that cross block boundaries, copy on write,
+//    reorder the batch and refuse a swapped-out sequence, both must write
+//    bit-identical outputs;
+//  * KVAppendBatch: appended K/V land byte-exact in their block slots;
+//  * PagedPrefillBatch: within the bf16 tolerance of per-position decodes.
 #include "qwenvl_paged/KVCacheManager.h"
 #include "qwenvl_paged/MemoryAllocator.h"
 #include "qwenvl_paged/PagedAttention.h"
@@ -12,6 +15,7 @@
 
 #include "harness.h"
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
 #include <vector>
@@ -144,12 +148,108 @@ NATIVE_TEST(resident_tables_decode_bit_identical_to_the_per_step_flatten) {
     cudaFree(o2);
 }
 
+// bf16 bits of a seeded value for (sequence, token, stream, head, dim)
+bfloat16 kv_value(SequenceId s, std::uint32_t t, std::uint32_t stream, std::uint32_t h, std::uint32_t d) {
+    std::uint32_t m = 2166136261u;
+    for (std::uint32_t part : {static_cast<std::uint32_t>(s), t, stream, h, d}) m = (m ^ part) * 16777619u;
+    return bfloat16(static_cast<float>(m % 2000u) / 1000.0f - 1.0f);
+}
+
+// Writes every prompt token's K/V with KVAppendBatch (one launch per token
+// position, all sequences that have it), checks the bytes landed in their
+// slots, then prefills the prompts with PagedPrefillBatch and compares with
+// the single-sequence decode at each position.
+NATIVE_TEST(kv_append_places_tokens_and_prefill_matches_per_position_decode) {
+    constexpr std::uint32_t kBlocks = 64;
+    MemoryAllocator m(config(kBlocks));
+    KVCacheManager cache(m);
+    const std::vector<std::uint32_t> ctx = {20, 33, 16, 1};
+    const std::size_t B = ctx.size();
+    for (std::size_t b = 0; b < B; ++b) {
+        CHECK(cache.create_sequence(SequenceMetadata{b + 1, b + 1, {}, {}}));
+        CHECK(cache.reserve_tokens(b + 1, ctx[b]));
+    }
+    const std::size_t row = static_cast<std::size_t>(kH) * kD;  // one token of one stream
+    void *kd = nullptr, *vd = nullptr;
+    CHECK(cudaMalloc(&kd, B * row * 2) == cudaSuccess && cudaMalloc(&vd, B * row * 2) == cudaSuccess);
+    KVAppendBatch append(m);
+    const std::uint32_t max_ctx = *std::max_element(ctx.begin(), ctx.end());
+    for (std::uint32_t t = 0; t < max_ctx; ++t) {
+        std::vector<CacheView> views;
+        std::vector<std::uint32_t> pos;
+        std::vector<bfloat16> kh, vh;
+        for (std::size_t b = 0; b < B; ++b) {
+            if (t >= ctx[b]) continue;
+            CHECK(cache.ensure_token_writable(b + 1, t).has_value());
+            views.push_back(*cache.cache_view(b + 1));
+            pos.push_back(t);
+            for (std::uint32_t h = 0; h < kH; ++h)
+                for (std::uint32_t d = 0; d < kD; ++d) {
+                    kh.push_back(kv_value(b + 1, t, 0, h, d));
+                    vh.push_back(kv_value(b + 1, t, 1, h, d));
+                }
+        }
+        cudaMemcpy(kd, kh.data(), kh.size() * 2, cudaMemcpyHostToDevice);
+        cudaMemcpy(vd, vh.data(), vh.size() * 2, cudaMemcpyHostToDevice);
+        CHECK(append.run(views, pos, 0, kd, vd));
+        CHECK(m.synchronize());  // the host buffers above are reused next token
+    }
+    CHECK(append.device_error() == 0);
+
+    // every token's K and V sit at their slots
+    KVBlockLayout layout;
+    layout.shape = m.block_shape();
+    std::vector<std::uint16_t> blk(m.block_shape().byte_size() / 2);
+    for (std::size_t b = 0; b < B; ++b) {
+        const auto v = cache.cache_view(b + 1);
+        for (std::uint32_t t = 0; t < ctx[b]; ++t) {
+            const PhysicalBlockId id = *v->block_table->lookup(t / kT);
+            CHECK(m.read_bytes(id, 0, blk.data(), blk.size() * 2));
+            for (std::uint32_t st = 0; st < 2; ++st)
+                for (std::uint32_t h = 0; h < kH; ++h) {
+                    const std::size_t off =
+                        *layout.element_offset(0, st == 0 ? KVStream::Key : KVStream::Value, t % kT, h);
+                    for (std::uint32_t d = 0; d < kD; ++d) CHECK(blk[off + d] == kv_value(b + 1, t, st, h, d).bits);
+                }
+        }
+    }
+
+    // prefill of the whole prompts against the decode at each position
+    const std::size_t qrow = static_cast<std::size_t>(kHQ) * kD;
+    std::vector<bfloat16> q(B * max_ctx * qrow);
+    for (std::size_t k = 0; k < q.size(); ++k) q[k] = bfloat16(mix(11u, static_cast<std::uint32_t>(k)));
+    void *qd = nullptr, *od = nullptr;
+    CHECK(cudaMalloc(&qd, q.size() * 2) == cudaSuccess && cudaMalloc(&od, q.size() * 2) == cudaSuccess);
+    cudaMemcpy(qd, q.data(), q.size() * 2, cudaMemcpyHostToDevice);
+    std::vector<CacheView> views;
+    for (std::size_t b = 0; b < B; ++b) views.push_back(*cache.cache_view(b + 1));
+    const float scale = 1.f / std::sqrt(static_cast<float>(kD));
+    PagedPrefillBatch prefill(m);
+    CHECK(prefill.run(views, ctx, ctx, 0, kHQ, scale, qd, od));
+    CHECK(prefill.device_error() == 0);
+    std::vector<bfloat16> got(q.size());
+    cudaMemcpy(got.data(), od, got.size() * 2, cudaMemcpyDeviceToHost);
+    std::vector<bfloat16> want(qrow);
+    for (std::size_t b = 0; b < B; ++b)
+        for (std::uint32_t t = 0; t < ctx[b]; ++t) {
+            const bfloat16* qp = q.data() + (b * max_ctx + t) * qrow;
+            CHECK(paged_attention_decode<bfloat16>(views[b], qp, PagedAttentionParams{0, kHQ, t + 1, scale},
+                                                   want.data()));
+            for (std::size_t k = 0; k < qrow; ++k)
+                CHECK_NEAR(static_cast<float>(got[(b * max_ctx + t) * qrow + k]), static_cast<float>(want[k]), 2e-2);
+        }
+    cudaFree(kd);
+    cudaFree(vd);
+    cudaFree(qd);
+    cudaFree(od);
+}
+
 }  // namespace
 
-extern "C" __attribute__((visibility("default"))) int qvp_residentchecks_list(char* out, size_t cap) {
+extern "C" __attribute__((visibility("default"))) int qvp_hostlayerchecks_list(char* out, size_t cap) {
     return native::list_cases(out, cap);
 }
 
-extern "C" __attribute__((visibility("default"))) int qvp_residentchecks_run(const char* name, char* msg, size_t cap) {
+extern "C" __attribute__((visibility("default"))) int qvp_hostlayerchecks_run(const char* name, char* msg, size_t cap) {
     return native::run_case(name, msg, cap);
 }

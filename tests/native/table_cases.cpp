@@ -1,6 +1,7 @@
 // TEST INFRASTRUCTURE: host checks of this library's additions to the
 // reference interface: the resident block tables (qwenvl_paged/
-// ResidentTables.h) and host-visible pools (qwenvl_paged/Block.h). For the
+// ResidentTables.h), host-visible pools (qwenvl_paged/Block.h) and the
+// refusal rules of PagedPrefillBatch and KVAppendBatch. For the
 // tables, each packet the planner emits is applied to a host mirror of the
 // device table, the way qvp_scatter_blocks and the copy
 // of the context lengths apply it on the device, and after every step the
@@ -9,6 +10,7 @@
 // it runs on the CPU.
 #include "qwenvl_paged/KVCacheManager.h"
 #include "qwenvl_paged/MemoryAllocator.h"
+#include "qwenvl_paged/PagedAttention.h"
 #include "qwenvl_paged/ResidentTables.h"
 #include "qwenvl_paged/SwapBackend.h"
 
@@ -311,6 +313,61 @@ NATIVE_TEST(host_visible_pools_pad_the_stride_and_follow_the_process_setting) {
     CHECK(plain.block_stride() == config(8).block_shape.byte_size());
     CHECK(visible.block_stride() > config(8).block_shape.byte_size() && visible.block_stride() % 256 == 0);
     CHECK(visible.block(1)->size_bytes() == plain.block(1)->size_bytes());
+}
+
+// ---- prefill and KV-append batches: refusals before any device work -------
+
+void* const kFakeDevicePtr = reinterpret_cast<void*>(0x100000);  // never dereferenced: no storage
+
+NATIVE_TEST(prefill_batch_refuses_bad_query_lengths_and_unmapped_contexts) {
+    Engine e(64);
+    PagedPrefillBatch pb(e.alloc);
+    CHECK(e.cache.create_sequence(meta(1)) && e.cache.reserve_tokens(1, 40));
+    const std::vector<CacheView> v{*e.cache.cache_view(1)};
+    CHECK(!pb.run(v, {40}, {41}, 0, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));  // query past the context
+    CHECK(pb.last_error().find("query length") != std::string::npos);
+    CHECK(!pb.run(v, {40}, {0}, 0, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(!pb.run(v, {49}, {1}, 0, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));  // context past the mapped blocks
+    CHECK(pb.last_status() == 2);                                               // QVP_ERR_UNMAPPED
+    CHECK(!pb.run(v, {40}, {8}, 1, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));  // layer outside the shape
+    CHECK(!pb.run(v, {40}, {8}, 0, 3, 1.f, kFakeDevicePtr, kFakeDevicePtr));  // heads that do not group
+    CHECK(!pb.run(v, {40, 40}, {8}, 0, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(pb.run({}, {}, {}, 0, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));     // empty batch: nothing to do
+    // every check passes: stops at the missing device storage
+    CHECK(!pb.run(v, {40}, {40}, 0, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(pb.last_error().find("no device storage") != std::string::npos);
+    CHECK(e.cache.swap_out_sequence(1) == 3u);
+    const std::vector<CacheView> swapped{*e.cache.cache_view(1)};
+    CHECK(!pb.run(swapped, {40}, {1}, 0, 4, 1.f, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(pb.last_status() == 2);
+}
+
+NATIVE_TEST(kv_append_refuses_shared_read_only_and_unmapped_targets) {
+    Engine e(64);
+    KVAppendBatch ab(e.alloc);
+    CHECK(e.cache.create_sequence(meta(1)) && e.cache.reserve_tokens(1, kT + 1));
+    CHECK(e.cache.fork_sequence(1, meta(2)));
+    auto views = [&](std::initializer_list<SequenceId> ids) {
+        std::vector<CacheView> v;
+        for (SequenceId s : ids) v.push_back(*e.cache.cache_view(s));
+        return v;
+    };
+    // block 1 is shared by the fork: writing it would change both sequences
+    CHECK(!ab.run(views({1}), {kT}, 0, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(ab.last_error().find("shared or read-only") != std::string::npos);
+    CHECK(!ab.run(views({2}), {kT}, 0, kFakeDevicePtr, kFakeDevicePtr));
+    // position past the mapped blocks
+    CHECK(!ab.run(views({1}), {2 * kT}, 0, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(ab.last_status() == 2);
+    // layer outside the shape, count mismatch, null K
+    CHECK(!ab.run(views({1}), {kT}, 1, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(!ab.run(views({1, 2}), {kT}, 0, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(!ab.run(views({1}), {kT}, 0, nullptr, kFakeDevicePtr));
+    // after copy-on-write both targets are private and writable: the checks
+    // pass and the call stops at the missing device storage
+    CHECK(e.cache.ensure_token_writable(1, kT).has_value() && e.cache.ensure_token_writable(2, kT).has_value());
+    CHECK(!ab.run(views({1, 2}), {kT, kT}, 0, kFakeDevicePtr, kFakeDevicePtr));
+    CHECK(ab.last_error().find("no device storage") != std::string::npos);
 }
 
 }  // namespace
