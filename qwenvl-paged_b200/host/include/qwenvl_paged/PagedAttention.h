@@ -164,7 +164,8 @@ private:
 // first), otherwise nothing is written and run() returns false. `k` and `v`
 // are device arrays [batch][num_kv_heads][head_dim] in the pool's element
 // type. Enqueued on the allocator's stream after any queued copy-on-write
-// copies, one launch per call.
+// copies, one launch per call; the host work and the upload are one block id
+// and one slot per sequence.
 class KVAppendBatch {
 public:
     explicit KVAppendBatch(const MemoryAllocator& allocator);

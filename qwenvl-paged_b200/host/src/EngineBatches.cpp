@@ -202,32 +202,29 @@ bool KVAppendBatch::run(const std::vector<CacheView>& views, const std::vector<s
         error_ = "layer outside the block shape";
         return false;
     }
-    std::uint32_t pitch = 1;
+    // The kernel needs only each target block: a one-column table holding it,
+    // with the slot inside the block as the position. [ids B][slots B]
+    std::vector<std::int32_t> staged(2 * B);
     for (std::size_t b = 0; b < B; ++b) {
         if (views[b].allocator != allocator_ || !views[b].valid()) {
             error_ = "sequence " + std::to_string(b) + " is not a view of this allocator";
             return false;
         }
-        pitch = std::max<std::uint32_t>(pitch, positions[b] / tpb + 1);
-    }
-    // [tables B x pitch][positions B]
-    std::vector<std::int32_t> staged(B * pitch + B, -1);
-    for (std::size_t b = 0; b < B; ++b) {
-        const std::uint32_t blk = positions[b] / tpb;
-        if (!write_row(views[b], blk + 1, staged.data() + b * pitch)) {
+        const BlockTableEntry* e = views[b].block_table->entry(positions[b] / tpb);
+        if (e == nullptr || e->swap_slot.has_value() || e->physical_id >= allocator_->num_blocks()) {
             status_ = QVP_ERR_UNMAPPED;
-            error_ = "sequence " + std::to_string(b) + ": the target block or one before it is not mapped";
+            error_ = "sequence " + std::to_string(b) + ": the target block is not mapped";
             return false;
         }
         // a shared or read-only block would change every sequence that maps it
-        const BlockTableEntry* e = views[b].block_table->entry(blk);
         const PhysicalBlockInfo* in = allocator_->info(e->physical_id);
         if (!e->writable || in == nullptr || in->ref_count != 1) {
             error_ = "sequence " + std::to_string(b) +
                      ": the target block is shared or read-only (call ensure_token_writable first)";
             return false;
         }
-        staged[B * pitch + b] = static_cast<std::int32_t>(positions[b]);
+        staged[b] = static_cast<std::int32_t>(e->physical_id);
+        staged[B + b] = static_cast<std::int32_t>(positions[b] % tpb);
     }
     MemoryAllocator& alloc = const_cast<MemoryAllocator&>(*allocator_);
     if (!alloc.has_storage()) {
@@ -244,7 +241,7 @@ bool KVAppendBatch::run(const std::vector<CacheView>& views, const std::vector<s
     const qvp_block_shape shape{sh.tokens_per_block, sh.num_layers, sh.num_kv_heads, sh.head_dim,
                                 sh.bytes_per_element};
     status_ = qvp_kv_append(alloc.pool_base(), alloc.block_stride(), alloc.num_blocks(), &shape, layer,
-                            static_cast<std::uint32_t>(B), pitch, dev_buf_, dev_buf_ + B * pitch, k, v, error_word_,
+                            static_cast<std::uint32_t>(B), 1, dev_buf_, dev_buf_ + B, k, v, error_word_,
                             alloc.stream());
     if (status_ != QVP_OK) error_ = qvp_last_error();
     return status_ == QVP_OK;

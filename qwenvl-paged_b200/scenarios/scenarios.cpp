@@ -346,8 +346,8 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
 
 // cfg2-shaped engine loop through the C++ API: `batch` sequences with seeded
 // contexts in [lo, hi]. A step gives every sequence one more token (reserve
-// at a block boundary, then ensure_token_writable) and decodes the batch with
-// PagedDecodeBatch. The loop runs twice, with the block tables flattened and
+// at a block boundary, ensure_token_writable, KVAppendBatch writes the
+// token's K and V) and decodes the batch with PagedDecodeBatch. The loop runs twice, with the block tables flattened and
 // uploaded every step and with resident tables, each over `steps` timed steps
 // after `warmup`. Per mode it reports the wall time of a step (host
 // bookkeeping and decode, pipelined; the clock stops after the last decode
@@ -397,24 +397,31 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_engine(int ba
     }
     const std::size_t qel = static_cast<std::size_t>(batch) * hq * sh.head_dim;
     void* q = device_query(qel, seed + 1);
+    const std::size_t kvel = static_cast<std::size_t>(batch) * sh.num_kv_heads * sh.head_dim;
+    void* kd = device_query(kvel, seed + 2);
+    void* vd = device_query(kvel, seed + 3);
     void *o1 = nullptr, *o2 = nullptr;
     cudaMalloc(&o1, qel * 2);
     cudaMalloc(&o2, qel * 2);
     const float scale = 1.f / std::sqrt(128.f);
     bool ok = true;
+    KVAppendBatch append(alloc);
+    std::vector<std::uint32_t> positions(batch);
 
-    auto advance = [&]() {
-        for (int b = 0; b < batch; ++b) {
-            if (ctx[b] % T == 0) ok = cache.reserve_tokens(seqs[b], 1) && ok;
-            ok = cache.ensure_token_writable(seqs[b], ctx[b]).has_value() && ok;
-            ++ctx[b];
-        }
-    };
     auto views = [&]() {
         std::vector<CacheView> v;
         v.reserve(seqs.size());
         for (SequenceId s : seqs) v.push_back(*cache.cache_view(s));
         return v;
+    };
+    // one new token per sequence: map it, make it private, write its K/V
+    auto advance = [&]() {
+        for (int b = 0; b < batch; ++b) {
+            if (ctx[b] % T == 0) ok = cache.reserve_tokens(seqs[b], 1) && ok;
+            ok = cache.ensure_token_writable(seqs[b], ctx[b]).has_value() && ok;
+            positions[b] = ctx[b]++;
+        }
+        ok = append.run(views(), positions, 0, kd, vd) && ok;
     };
     auto alg_bytes = [&]() {
         double kv = 0, tbl = 0;
@@ -477,7 +484,10 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_engine(int ba
     cudaMemcpy(a.data(), o1, a.size(), cudaMemcpyDeviceToHost);
     cudaMemcpy(b.data(), o2, b.size(), cudaMemcpyDeviceToHost);
     const bool same = std::memcmp(a.data(), b.data(), a.size()) == 0;
+    const int append_error = append.device_error();
     cudaFree(q);
+    cudaFree(kd);
+    cudaFree(vd);
     cudaFree(o1);
     cudaFree(o2);
 
@@ -495,6 +505,7 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_engine(int ba
     js << ", ";
     mode("resident_tables", rr);
     js << ", \"resident_gbs\": " << rr.gbs << ", \"outputs_identical\": " << (same ? "true" : "false")
-       << ", \"all_ok\": " << (ok ? "true" : "false") << "}";
+       << ", \"append_device_error\": " << append_error << ", \"all_ok\": " << (ok ? "true" : "false")
+       << ", \"step\": \"reserve + ensure_token_writable + KVAppendBatch + PagedDecodeBatch\"}";
     return emit(js.str(), out, cap);
 }
