@@ -244,6 +244,63 @@ NATIVE_TEST(kv_append_places_tokens_and_prefill_matches_per_position_decode) {
     cudaFree(od);
 }
 
+// Copy-on-write ordering on real bytes: a branch appends into the shared
+// last block, so ensure_token_writable queues a copy and KVAppendBatch must
+// land it before writing the new token. The branch's private block then holds
+// the parent's earlier tokens plus its own; the parent's block is unchanged.
+NATIVE_TEST(kv_append_after_copy_on_write_keeps_the_parent_block_intact) {
+    MemoryAllocator m(config(16));
+    KVCacheManager cache(m);
+    CHECK(cache.create_sequence(SequenceMetadata{1, 1, {}, {}}) && cache.reserve_tokens(1, 8));
+    const std::size_t row = static_cast<std::size_t>(kH) * kD;
+    void *kd = nullptr, *vd = nullptr;
+    CHECK(cudaMalloc(&kd, 2 * row * 2) == cudaSuccess && cudaMalloc(&vd, 2 * row * 2) == cudaSuccess);
+    KVAppendBatch append(m);
+    auto put = [&](const std::vector<SequenceId>& seqs, std::uint32_t t) {
+        std::vector<CacheView> views;
+        std::vector<std::uint32_t> pos;
+        std::vector<bfloat16> kh, vh;
+        for (SequenceId s : seqs) {
+            CHECK(cache.ensure_token_writable(s, t).has_value());
+            views.push_back(*cache.cache_view(s));
+            pos.push_back(t);
+            for (std::uint32_t h = 0; h < kH; ++h)
+                for (std::uint32_t d = 0; d < kD; ++d) {
+                    kh.push_back(kv_value(s, t, 0, h, d));
+                    vh.push_back(kv_value(s, t, 1, h, d));
+                }
+        }
+        cudaMemcpy(kd, kh.data(), kh.size() * 2, cudaMemcpyHostToDevice);
+        cudaMemcpy(vd, vh.data(), vh.size() * 2, cudaMemcpyHostToDevice);
+        CHECK(append.run(views, pos, 0, kd, vd));
+        CHECK(m.synchronize());
+    };
+    for (std::uint32_t t = 0; t < 7; ++t) put({1}, t);
+    CHECK(cache.fork_sequence(1, SequenceMetadata{2, 1, {}, {}}));
+    const PhysicalBlockId shared = *cache.cache_view(1)->block_table->lookup(0);
+    put({2}, 7);  // the branch copies block 0, then writes token 7 into its copy
+    put({1}, 7);  // the parent now holds block 0 alone and writes in place
+    const PhysicalBlockId mine = *cache.cache_view(2)->block_table->lookup(0);
+    CHECK(mine != shared && *cache.cache_view(1)->block_table->lookup(0) == shared);
+    CHECK(append.device_error() == 0);
+    KVBlockLayout layout;
+    layout.shape = m.block_shape();
+    std::vector<std::uint16_t> blk(m.block_shape().byte_size() / 2);
+    for (const auto& [id, owner] : {std::pair<PhysicalBlockId, SequenceId>{shared, 1}, {mine, 2}}) {
+        CHECK(m.read_bytes(id, 0, blk.data(), blk.size() * 2));
+        for (std::uint32_t t = 0; t < 8; ++t)
+            for (std::uint32_t st = 0; st < 2; ++st)
+                for (std::uint32_t h = 0; h < kH; ++h) {
+                    const std::size_t off = *layout.element_offset(0, st == 0 ? KVStream::Key : KVStream::Value, t, h);
+                    // tokens 0..6 are the parent's in both blocks; token 7 is each block's own
+                    const SequenceId src = t < 7 ? 1 : owner;
+                    for (std::uint32_t d = 0; d < kD; ++d) CHECK(blk[off + d] == kv_value(src, t, st, h, d).bits);
+                }
+    }
+    cudaFree(kd);
+    cudaFree(vd);
+}
+
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) int qvp_hostlayerchecks_list(char* out, size_t cap) {
