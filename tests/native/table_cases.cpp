@@ -1,13 +1,14 @@
 // TEST INFRASTRUCTURE: host checks of this library's additions to the
 // reference interface: the resident block tables (qwenvl_paged/
-// ResidentTables.h), host-visible pools (qwenvl_paged/Block.h) and the
-// refusal rules of PagedPrefillBatch and KVAppendBatch. For the
+// ResidentTables.h), host-visible pools (qwenvl_paged/Block.h), the refusal
+// rules of PagedPrefillBatch and KVAppendBatch, and LruEvictionPolicy. For the
 // tables, each packet the planner emits is applied to a host mirror of the
 // device table, the way qvp_scatter_blocks and the copy
 // of the context lengths apply it on the device, and after every step the
 // mirror must hold, for every sequence, the same ids over its context as a
 // full per-step flatten of its BlockTable. Bookkeeping-only pools, so all of
 // it runs on the CPU.
+#include "qwenvl_paged/EvictionPolicy.h"
 #include "qwenvl_paged/KVCacheManager.h"
 #include "qwenvl_paged/MemoryAllocator.h"
 #include "qwenvl_paged/PagedAttention.h"
@@ -368,6 +369,50 @@ NATIVE_TEST(kv_append_refuses_shared_read_only_and_unmapped_targets) {
     CHECK(e.cache.ensure_token_writable(1, kT).has_value() && e.cache.ensure_token_writable(2, kT).has_value());
     CHECK(!ab.run(views({1, 2}), {kT, kT}, 0, kFakeDevicePtr, kFakeDevicePtr));
     CHECK(ab.last_error().find("no device storage") != std::string::npos);
+}
+
+// ---- LruEvictionPolicy ------------------------------------------------------
+
+NATIVE_TEST(eviction_policy_names_the_least_recently_decoded_private_block) {
+    Engine e(64);
+    LruEvictionPolicy policy(e.cache);
+    e.alloc.set_eviction_selector(policy.selector());
+    for (SequenceId s = 1; s <= 3; ++s) CHECK(e.cache.create_sequence(meta(s)) && e.cache.reserve_tokens(s, 40));
+    auto view = [&](SequenceId s) { return *e.cache.cache_view(s); };
+    CHECK(!e.alloc.select_eviction_candidate());  // nothing decoded yet
+    policy.touch({view(1), view(2)});
+    CHECK(!e.alloc.select_eviction_candidate());  // 1 and 2 are in the current batch; 3 never decoded
+    policy.touch({view(2), view(3)});
+    // 1 is the oldest outside the batch: its last block
+    CHECK(e.alloc.select_eviction_candidate() == view(1).block_table->lookup(2));
+    policy.touch({view(3)});
+    // 1 (step 1) is older than 2 (step 2)
+    CHECK(e.alloc.select_eviction_candidate() == view(1).block_table->lookup(2));
+    // shared blocks are skipped: fork 1, so its blocks are held twice
+    CHECK(e.cache.fork_sequence(1, meta(4)));
+    CHECK(e.alloc.select_eviction_candidate() == view(2).block_table->lookup(2));
+    // copy-on-write makes 1's last block private again
+    CHECK(e.cache.ensure_token_writable(1, 39).has_value());
+    CHECK(e.alloc.select_eviction_candidate() == view(1).block_table->lookup(2));
+    // a swapped-out sequence has no frame to name; a released one is skipped
+    CHECK(e.cache.swap_out_sequence(2) > 0u);
+    e.cache.release_sequence(1);
+    // left: 2 swapped out, 3 in the current batch, 4 never decoded
+    CHECK(!e.alloc.select_eviction_candidate());
+}
+
+NATIVE_TEST(eviction_policy_advice_drives_a_swap_out_that_frees_the_block) {
+    Engine e(8);
+    LruEvictionPolicy policy(e.cache);
+    e.alloc.set_eviction_selector(policy.selector());
+    for (SequenceId s = 1; s <= 2; ++s) CHECK(e.cache.create_sequence(meta(s)) && e.cache.reserve_tokens(s, 64));
+    CHECK(!e.alloc.can_allocate(1));
+    policy.touch({*e.cache.cache_view(1)});
+    policy.touch({*e.cache.cache_view(2)});
+    const auto victim = e.alloc.select_eviction_candidate();
+    CHECK(victim.has_value() && *victim == *e.cache.cache_view(1)->block_table->lookup(3));
+    CHECK(e.cache.swap_out_sequence(1) == 4u && e.alloc.can_allocate(4));
+    CHECK(e.alloc.info(*victim)->state == BlockState::Free);
 }
 
 }  // namespace
