@@ -370,6 +370,7 @@ def run_ours(args):
                 "split_tokens": plan["split_tokens"],
                 "num_splits_max": plan["num_splits"],
                 "kernel": kernel_name,
+                "combine_threads": args.combine_threads if plan["stream"] else None,
                 "l2": f"inputs larger than L2 ({w.kv_bytes() / 1e6:.0f} MB of K/V read per step)",
                 "parallelism": f"dp{world}" if scaling == "weak" else
                 (f"kv-head shards x{w.meta.get('head_parts', world)} x sequence shards x{w.meta.get('batch_parts', 1)}")
@@ -727,9 +728,13 @@ def main():
                    help="multi-GPU cfg4: capture decode + all-gather in a CUDA graph (experimental)")
     p.add_argument("--shard", choices=["hybrid", "heads"], default="hybrid",
                    help="cfg4 over N GPUs: kv heads only, or kv heads (>= 4 per GPU) then sequences")
+    p.add_argument("--combine-threads", type=int, choices=[64, 128, 256], default=256,
+                   help="CTA size of the stream-K combine (QVP_COMBINE_THREADS)")
     p.add_argument("--profile", action="store_true",
                    help="for ncu: only warm-up and timed decode steps (no clock probe, e2e or CPU baseline)")
     args = p.parse_args()
+    # read by libqvp at its first combine launch
+    os.environ["QVP_COMBINE_THREADS"] = str(args.combine_threads)
     if args.warmup < 3:
         args.warmup = 3
     if args.workload == "prefill" and args.impl == "ours":

@@ -30,6 +30,7 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 namespace qvp {
@@ -653,16 +654,18 @@ constexpr int kCombineWarps = kCombineThreads / 32;
 constexpr int kFewParts = 16;  // partials merged by the one-round-trip path
 
 // Merges the stream-K records of each (segment, kv head) into the output:
-// grid.x = nseg * HH, 256 threads. Launched as a programmatic dependent of
+// grid.x = nseg * HH, THREADS threads. Launched as a programmatic dependent of
 // paged_decode_stream; it waits for that grid (griddepcontrol.wait) before
-// reading anything. The eight warps split the segment's partial records
-// (warp w takes partials w, w+8, ...) when there are more than kFewParts of
-// them; each lane keeps its share of the
+// reading anything. THREADS (256 by default; 64 or 128 with
+// QVP_COMBINE_THREADS) sets the CTA size: smaller CTAs fit more of the grid
+// into one wave. The warps split the segment's partial records
+// (warp w takes partials w, w + warps, ...) when there are more than
+// kFewParts of them; each lane keeps its share of the
 // G x D outputs in registers and issues all of a partial's loads at once;
 // the warps' sums meet in shared memory. Dynamic shared memory:
-// kCombineWarps * G * D floats.
-template <int D, int HH, int J>
-__global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const float* __restrict__ rec_acc,
+// (THREADS / 32) * G * D floats.
+template <int D, int HH, int J, int THREADS = kCombineThreads>
+__global__ void __launch_bounds__(THREADS, 512 / THREADS) combine_records(const float* __restrict__ rec_acc,
                                                                    const float2* __restrict__ rec_ml,
                                                                    const int32_t* __restrict__ seg_prefix,
                                                                    __nv_bfloat16* __restrict__ out, uint32_t nseg,
@@ -671,8 +674,8 @@ __global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const floa
     constexpr int D4 = D / 4;
     constexpr int kMaxOut = 16 * D4 / 32;  // float4 outputs per lane for G = 16
     extern __shared__ float4 partial_sums[];  // [warps][G * D4]
-    __shared__ float s_max[kCombineWarps][16];
-    __shared__ float s_sum[kCombineWarps][16];
+    __shared__ float s_max[(THREADS / 32)][16];
+    __shared__ float s_sum[(THREADS / 32)][16];
     grid_dependency_wait();
     // the next decode may start its prologue while this grid runs
     grid_launch_dependents();
@@ -704,7 +707,7 @@ __global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const floa
         __shared__ float2 sml[16][kFewParts];
         __shared__ float sw[16][kFewParts];
         __shared__ float sinv[16];
-        for (int i = threadIdx.x; i < G * nparts; i += kCombineThreads) {
+        for (int i = threadIdx.x; i < G * nparts; i += THREADS) {
             const int r = i / nparts, k = i % nparts;
             sml[r][k] = usable(k) ? rec_ml[rec_of(k) * G + r] : make_float2(-INFINITY, 0.f);
         }
@@ -723,7 +726,7 @@ __global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const floa
             sinv[r] = 1.f / L;
         }
         __syncthreads();
-        for (int o = threadIdx.x; o < nout; o += kCombineThreads) {
+        for (int o = threadIdx.x; o < nout; o += THREADS) {
             const int r = o / D4;
             float4 v[kFewParts];
 #pragma unroll
@@ -752,13 +755,13 @@ __global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const floa
     // per-row maximum over this warp's partials (lane r holds row r)
     float m = -INFINITY;
     if (lane < G)
-        for (int k = warp; k < nparts; k += kCombineWarps)
+        for (int k = warp; k < nparts; k += (THREADS / 32))
             if (usable(k)) m = fmaxf(m, rec_ml[rec_of(k) * G + lane].x);
     if (lane < 16) s_max[warp][lane] = m;
     __syncthreads();
     float M = -INFINITY;
     if (lane < G)
-        for (int w = 0; w < kCombineWarps; ++w) M = fmaxf(M, s_max[w][lane]);
+        for (int w = 0; w < (THREADS / 32); ++w) M = fmaxf(M, s_max[w][lane]);
 
     // outputs in chunks of kChunk float4 per lane (all of a partial's loads
     // for one chunk are issued together)
@@ -769,7 +772,7 @@ __global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const floa
         float4 acc[kChunk];
 #pragma unroll
         for (int i = 0; i < kChunk; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = warp; k < nparts; k += kCombineWarps) {
+        for (int k = warp; k < nparts; k += (THREADS / 32)) {
             if (!usable(k)) continue;
             const size_t rec = rec_of(k);
             // weight of row `lane` in this partial, shared with the warp by shfl
@@ -806,11 +809,11 @@ __global__ void __launch_bounds__(kCombineThreads, 2) combine_records(const floa
     }
     if (lane < 16) s_sum[warp][lane] = lsum;
     __syncthreads();
-    for (int o = threadIdx.x; o < nout; o += kCombineThreads) {
+    for (int o = threadIdx.x; o < nout; o += THREADS) {
         const int r = o / D4;
         float L = 0.f;
         float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int w = 0; w < kCombineWarps; ++w) {
+        for (int w = 0; w < (THREADS / 32); ++w) {
             L += s_sum[w][r];
             const float4 v = partial_sums[w * nout + o];
             a.x += v.x;
@@ -1088,19 +1091,55 @@ int launch_fast(const qvp_decode_args& a, const DecodePlan& plan, const FastPara
     }
 }
 
+// CTA size of the combine: kCombineThreads unless QVP_COMBINE_THREADS is 64
+// or 128 (read once per process).
+int combine_threads() {
+    static const int threads = [] {
+        const char* v = std::getenv("QVP_COMBINE_THREADS");
+        const int n = v != nullptr ? std::atoi(v) : 0;
+        return (n == 64 || n == 128) ? n : kCombineThreads;
+    }();
+    return threads;
+}
+
+// The combine is a programmatic dependent: it may be scheduled while the
+// decode grid still runs and waits (griddepcontrol.wait) for its results.
+template <int D, int HH, int J, int THREADS>
+int launch_combine(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
+    constexpr int kWarps = THREADS / 32;
+    static std::atomic<std::uint64_t> attr_done{0};
+    auto kern = combine_records<D, HH, J, THREADS>;
+    const int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern),
+                                       kWarps * 16 * D * static_cast<int>(sizeof(float)), "cudaFuncSetAttribute(combine)");
+    if (rc != QVP_OK) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(sp.nseg * HH);
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = static_cast<size_t>(kWarps) * sp.group * D * sizeof(float);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return check_cuda(cudaLaunchKernelEx(&cfg, kern, static_cast<const float*>(sp.rec_acc),
+                                         static_cast<const float2*>(sp.rec_ml),
+                                         static_cast<const int32_t*>(sp.seg_prefix),
+                                         static_cast<__nv_bfloat16*>(a.out), sp.nseg, sp.head_groups, sp.hq,
+                                         sp.group, plan.grid_ctas),
+                      "launch combine_records");
+}
+
 template <int D, int HH, int STAGES>
 int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
     using S = FastShape<D, HH, STAGES>;
     constexpr int J = S::J;
     constexpr uint32_t kMaxSmem = S::kSmem + (kStreamMaxSegments + 1) * 4;
     static_assert(kMaxSmem <= 232448, "stream decode exceeds the 227 KB shared-memory limit");
-    static std::atomic<std::uint64_t> attr_done{0}, combine_attr_done{0};
+    static std::atomic<std::uint64_t> attr_done{0};
     auto kern = paged_decode_stream<D, HH, STAGES>;
     int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern), static_cast<int>(kMaxSmem),
                                  "cudaFuncSetAttribute(stream decode)");
-    if (rc != QVP_OK) return rc;
-    rc = set_smem_limit_once(combine_attr_done, reinterpret_cast<const void*>(combine_records<D, HH, J>),
-                             kCombineWarps * 16 * D * static_cast<int>(sizeof(float)), "cudaFuncSetAttribute(combine)");
     if (rc != QVP_OK) return rc;
     CUtensorMap map;
     rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
@@ -1123,24 +1162,11 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
         if (rc != QVP_OK) return rc;
     }
 
-    // The combine is a programmatic dependent: it may be scheduled while the
-    // decode grid still runs and waits (griddepcontrol.wait) for its results.
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(sp.nseg * HH);
-    cfg.blockDim = dim3(kCombineThreads);
-    cfg.dynamicSmemBytes = static_cast<size_t>(kCombineWarps) * sp.group * D * sizeof(float);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return check_cuda(cudaLaunchKernelEx(&cfg, combine_records<D, HH, J>, static_cast<const float*>(sp.rec_acc),
-                                         static_cast<const float2*>(sp.rec_ml),
-                                         static_cast<const int32_t*>(sp.seg_prefix),
-                                         static_cast<__nv_bfloat16*>(a.out), sp.nseg, sp.head_groups, sp.hq,
-                                         sp.group, plan.grid_ctas),
-                      "launch combine_records");
+    switch (combine_threads()) {
+        case 64: return launch_combine<D, HH, J, 64>(a, plan, sp, st);
+        case 128: return launch_combine<D, HH, J, 128>(a, plan, sp, st);
+        default: return launch_combine<D, HH, J, kCombineThreads>(a, plan, sp, st);
+    }
 }
 
 int launch_stream(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
