@@ -123,3 +123,32 @@ def bf16_f32(q: np.ndarray) -> np.ndarray:
 
 def mean_ctx(ctx) -> float:
     return float(np.mean(ctx)) if len(ctx) else math.nan
+
+
+class NativeCases:
+    """A native test library built on tests/native/harness.h: `<prefix>_list`
+    names its cases, `<prefix>_run(name)` runs one (0 = passed, failure text
+    otherwise)."""
+
+    def __init__(self, path: str, prefix: str):
+        self.path, self.prefix = path, prefix
+
+    def _lib(self):
+        import ctypes as C
+        return C.CDLL(self.path)
+
+    def names(self):
+        import ctypes as C
+        import os
+        if not os.path.exists(self.path):
+            return []
+        buf = C.create_string_buffer(1 << 16)
+        getattr(self._lib(), f"{self.prefix}_list")(buf, len(buf))
+        return [n for n in buf.value.decode().splitlines() if n]
+
+    def run(self, name: str):
+        """(return code, message) of one case."""
+        import ctypes as C
+        msg = C.create_string_buffer(4096)
+        rc = getattr(self._lib(), f"{self.prefix}_run")(name.encode(), msg, len(msg))
+        return rc, msg.value.decode()

@@ -8,25 +8,16 @@ PagedPrefillBatch (within the bf16 tolerance of per-position decodes).
 Not collected yet (no test_ prefix): run it on a GPU with
 `python -m pytest tests/host_layer_gpu_checks.py -q`, then rename it to
 test_host_layer_gpu.py."""
-import ctypes as C
 import os
 
 import pytest
 
-LIB = os.path.join(os.path.dirname(__file__), "native", "libqvp_hostlayer_checks.so")
+from helpers import NativeCases
 
-
-def _names():
-    if not os.path.exists(LIB):
-        return []
-    buf = C.create_string_buffer(1 << 16)
-    C.CDLL(LIB).qvp_hostlayerchecks_list(buf, len(buf))
-    return [n for n in buf.value.decode().splitlines() if n]
-
+CASES = NativeCases(os.path.join(os.path.dirname(__file__), "native", "libqvp_hostlayer_checks.so"), "qvp_hostlayerchecks")
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("name", _names())
+@pytest.mark.parametrize("name", CASES.names())
 def test_host_layer_check(name):
-    msg = C.create_string_buffer(4096)
-    rc = C.CDLL(LIB).qvp_hostlayerchecks_run(name.encode(), msg, len(msg))
-    assert rc == 0, msg.value.decode()
+    rc, msg = CASES.run(name)
+    assert rc == 0, msg
