@@ -69,22 +69,32 @@ def dist_env():
         os.environ.get("LOCAL_RANK", "0"))
 
 
-def make_workload(name, rank, world, gpus, args_shard="hybrid"):
+def make_workload(name, world, shard_mode="hybrid", emulate=0):
+    """(workload this rank holds, scaling, head_parts, batch_parts).
+
+    cfg2 over N GPUs splits by kv head first (head_parts = min(N, 4), the 4
+    kv heads), then by sequence (batch_parts = N / head_parts). Every GPU
+    keeps cfg2's bytes: a head group of head_parts GPUs decodes 64*head_parts
+    sequences, each GPU its 4/head_parts kv heads of them (weak scaling).
+    `emulate` = H runs, on one GPU, the workload one GPU of an H-way head split
+    holds (no collective), for profiling."""
     if name == "cfg2":
-        # weak scaling: every rank gets the same shape of work (same context
-        # lengths); the K/V/Q values differ per rank (device seed below)
-        return W.cfg2(seed=2), "weak"
+        hp = emulate if (emulate and world == 1) else min(world, 4)
+        if world % min(world, 4) != 0:
+            raise SystemExit(f"cfg2 runs on 1, 2, 4 or 8 GPUs, not {world}")
+        return W.cfg2_shard(hp), "weak", (hp if world > 1 else 1), world // min(world, 4)
     if name == "cfg1":
-        return W.cfg1(seed=1), "weak"
+        return W.cfg1(seed=1), "weak", 1, world
     if name == "cfg4":
-        if args_shard == "heads":
-            return W.cfg4(shards=max(world, 1)), "strong"
+        if shard_mode == "heads" or (emulate and world == 1):
+            n = emulate if (emulate and world == 1) else max(world, 1)
+            return W.cfg4(shards=n), "strong", (n if world > 1 else 1), 1
         # kv heads split while every GPU keeps >= 4 of them, then sequences
         import sharding
         hp, dp = sharding.hybrid_grid(8, 32, max(world, 1))
         w = W.cfg4(shards=hp, batch=32 // dp)
         w.meta.update({"head_parts": hp, "batch_parts": dp})
-        return w, "strong"
+        return w, "strong", hp, dp
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -141,6 +151,8 @@ class ClockSampler:
 
 
 def run_ours(args):
+    import ctypes
+
     import torch
 
     import qvp
@@ -151,17 +163,19 @@ def run_ours(args):
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
-    w, scaling = make_workload(args.workload, rank, world, args.gpus, args.shard)
+    w, scaling, hp, dp = make_workload(args.workload, world, args.shard, args.emulate_shards)
+    head_part, batch_part = rank % hp, rank // hp
+    sharded = hp > 1
     torch_dtype = torch.bfloat16 if w.dtype == "bf16" else torch.float32
 
-    # inputs generated on the device from a seed, resident in HBM
+    # inputs generated on the device from a seed, resident in HBM; every rank
+    # holds different K/V/Q values (its own heads, or its own sequences)
     g = torch.Generator(device=dev)
     g.manual_seed(w.seed * 1000 + 7 + 7919 * rank)
     pool = torch.zeros(w.num_blocks * w.block_stride // w.elem, dtype=torch_dtype, device=dev)
     pool.view(w.num_blocks, -1)[:, : w.block_bytes // w.elem].normal_(generator=g)
     q = torch.randn(w.batch, w.num_query_heads, w.head_dim, generator=g, device=dev, dtype=torch.float32).to(
         torch_dtype)
-    out = torch.empty_like(q)
     ctx_d = torch.from_numpy(w.context_lens).to(dev)
     tab_d = torch.from_numpy(w.tables).to(dev)
     err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -171,7 +185,11 @@ def run_ours(args):
                         num_query_heads=w.num_query_heads, scale=w.scale, batch=w.batch,
                         max_blocks_per_seq=w.pitch, max_context_len=w.max_context_len,
                         block_tables=tab_d.data_ptr(), context_lens=ctx_d.data_ptr(), query=q.data_ptr(),
-                        out=out.data_ptr(), split_tokens=args.split, error_word=err.data_ptr())
+                        out=0, split_tokens=args.split, error_word=err.data_ptr())
+    # `out` is what the step hands its consumer: this GPU's heads when the
+    # batch is not split by head, every head of its sequences when it is
+    out = torch.empty((w.batch, w.num_query_heads * hp, w.head_dim), dtype=torch_dtype, device=dev)
+    a.out = out.data_ptr()
     plan = qvp.decode_plan(a)
     ws = None
     if plan["workspace_bytes"]:
@@ -181,27 +199,42 @@ def run_ours(args):
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
     launches_per_step = 2 if plan["stream"] else 1 + (1 if plan["num_splits"] > 1 else 0)
-    # (the NCCL all-gather of cfg4 shards is a library collective, not counted)
     kernel_name = ("paged_decode_stream (persistent stream-K, TMA + mma.sync) + combine_records" if plan["stream"]
                    else "paged_decode_fast (grid split-K, TMA + mma.sync) + combine_partitions" if plan["fast"]
                    else "paged_decode_generic + combine_partitions")
 
-    gather = scaling == "strong" and world > 1 and not args.no_gather
-    hp, dp = w.meta.get("head_parts", world), w.meta.get("batch_parts", 1)
-    if gather:
-        import sharding
-        g_buf = torch.empty((dp, hp) + tuple(out.shape), dtype=out.dtype, device=dev)
-        g_out = torch.empty((dp * out.shape[0], hp * out.shape[1], out.shape[2]), dtype=out.dtype, device=dev)
+    comm = None
+    if sharded and not args.no_gather:
+        # one NCCL communicator per head group (the hp GPUs that share a batch),
+        # made by libqvp; the unique id travels over torch.distributed
+        import torch.distributed as dist
+        ids = [None] * world
+        dist.all_gather_object(ids, qvp.nccl_unique_id() if head_part == 0 else None)
+        comm = qvp.nccl_comm_init(ids[batch_part * hp], hp, head_part)
+        launches_per_step += 1  # reassemble_kernel (the NCCL all-gather is a library collective, not counted)
+
+    def shard_args(decode_args, out_ptr, gathered_ptr):
+        return qvp.shard_decode_args(decode_args, head_part, hp, local, comm, gathered_ptr, out_ptr)
+
+    gathered = []
+    sa = None
+    if comm is not None:
+        sa = shard_args(a, out.data_ptr(), 0)
+        gathered.append(torch.empty(qvp.shard_gather_bytes(sa), dtype=torch.uint8, device=dev))
+        sa.gathered = gathered[0].data_ptr()
+
+    def run_step(decode_args, shard_decode_args, st):
+        if shard_decode_args is not None:
+            rc = qvp.lib.qvp_shard_decode(ctypes.byref(shard_decode_args), st)
+            what = "qvp_shard_decode"
+        else:
+            rc = qvp.decode(decode_args, st)
+            what = "qvp_decode"
+        if rc != 0:
+            raise RuntimeError(f"{what} failed: {rc} {qvp.last_error()}")
 
     def step():
-        # the current stream: the caller's, or the capture stream of a graph
-        st = qvp.decode(a, torch.cuda.current_stream().cuda_stream)
-        if st != 0:
-            raise RuntimeError(f"qvp_decode failed: {st} {qvp.last_error()}")
-        if gather:
-            # a consumer that needs every output on every GPU: one NCCL
-            # all-gather of each rank's [B/dp, Hq/hp, D], reassembled
-            sharding.all_gather_hybrid(out, hp, dp, gathered=g_buf, result=g_out)
+        run_step(a, sa, sh)
 
     def barrier():
         if world > 1:
@@ -226,22 +259,6 @@ def run_ours(args):
             ms = float(t.item())
         return ms
 
-    if gather and args.graph:
-        # One step = decode + all-gather + reorder, a handful of launches a
-        # few tens of microseconds long: capture it once in a CUDA graph and
-        # replay it, so the host does not pace the GPUs.
-        for _ in range(3):
-            step()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, capture_error_mode="thread_local"):
-            step()
-        def step():  # noqa: F811
-            graph.replay()
-        graphed = True
-    else:
-        graphed = False
-
     sampler = ClockSampler(local)
     sampler.start()
     for _ in range(args.warmup):
@@ -249,11 +266,21 @@ def run_ours(args):
     torch.cuda.synchronize()
     total_ms = timed(step, args.steps)
     # Clocks: the timed region of a short run can be shorter than the sampling
-    # period, so keep the same step running untimed until ~1 s has elapsed.
-    t_end = time.time() + (0.0 if args.profile else 1.0)
-    while time.time() < t_end:
-        for _ in range(50):
+    # period, so keep the same step running untimed until ~1 s has elapsed
+    # (every rank runs the same number of extra steps: the collective matches).
+    n_extra = 0
+    if not args.profile:
+        per = max(total_ms / args.steps, 1e-3)
+        n_extra = int(1000.0 / per) + 1
+        if world > 1:
+            import torch.distributed as dist
+            t = torch.tensor([n_extra], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            n_extra = int(t.item())
+        for i in range(n_extra):
             step()
+            if i % 64 == 63:
+                torch.cuda.synchronize()
         torch.cuda.synchronize()
     sampler.stop()
     if int(err.item()) != 0:
@@ -274,11 +301,11 @@ def run_ours(args):
 
     # e2e through the C ABI with host buffers. Every step copies its own
     # inputs (block tables, context lengths and queries, packed in one pinned
-    # buffer) host -> device, runs qvp_decode and copies its outputs back to
-    # pinned host memory, all inside the timed region. As in a serving engine
-    # the copies run on two copy streams, double-buffered, so step k+1's
-    # upload and step k's download overlap step k's decode.
-    import ctypes
+    # buffer) host -> device, runs the decode (and, for kv-head shards, the
+    # all-gather of every head) and copies its outputs back to pinned host
+    # memory, all inside the timed region. As in a serving engine the copies
+    # run on two copy streams, double-buffered, so step k+1's upload and step
+    # k's download overlap step k's decode.
     nb_tab, nb_ctx = w.tables.nbytes, w.context_lens.nbytes
     nb_q = q.numel() * q.element_size()
     off_ctx = nb_tab
@@ -290,7 +317,7 @@ def run_ours(args):
     dev_in = [torch.empty_like(host_in, device=dev) for _ in range(2)]
     dev_out = [torch.empty_like(out) for _ in range(2)]
     host_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
-    args2 = []
+    args2, sargs2 = [], []
     for b in range(2):
         ab = qvp.DecodeArgs()
         ctypes.memmove(ctypes.byref(ab), ctypes.byref(a), ctypes.sizeof(a))
@@ -299,6 +326,11 @@ def run_ours(args):
         ab.query = dev_in[b].data_ptr() + off_q
         ab.out = dev_out[b].data_ptr()
         args2.append(ab)
+        if comm is not None:
+            gathered.append(torch.empty_like(gathered[0]))
+            sargs2.append(shard_args(ab, dev_out[b].data_ptr(), gathered[-1].data_ptr()))
+        else:
+            sargs2.append(None)
     up_s, down_s = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
     ev_up = [torch.cuda.Event() for _ in range(2)]
     ev_dec = [torch.cuda.Event() for _ in range(2)]
@@ -313,11 +345,7 @@ def run_ours(args):
             ev_up[b].record(up_s)
             stream.wait_event(ev_up[b])
             stream.wait_event(ev_down[b])  # step i-2's outputs have left buffer b
-            st = qvp.decode(args2[b], sh)
-            if st != 0:
-                raise RuntimeError(f"qvp_decode failed: {st} {qvp.last_error()}")
-            if gather:
-                sharding.all_gather_hybrid(dev_out[b], hp, dp, gathered=g_buf, result=g_out)
+            run_step(args2[b], sargs2[b], sh)
             ev_dec[b].record(stream)
             down_s.wait_event(ev_dec[b])
             with torch.cuda.stream(down_s):
@@ -335,14 +363,37 @@ def run_ours(args):
     h2d = q.numel() * q.element_size() + w.tables.nbytes + w.context_lens.nbytes
     d2h = out.numel() * out.element_size()
 
-    cpu = None
-    if rank == 0 and world == 1 and not (args.no_cpu or args.profile):
+    cpu = parity = None
+    if rank == 0 and world == 1 and not (args.no_cpu or args.profile or args.emulate_shards):
         host_pool = pool.view(torch.uint8).cpu().numpy() if w.elem == 2 else pool.cpu().numpy().view(np.uint8)
         host_q = q.cpu().view(torch.int16).numpy().view(np.uint16) if w.dtype == "bf16" else q.cpu().numpy()
-        cpu = cpu_baseline(w, host_pool.reshape(-1), host_q, budget_s=args.cpu_budget)
+        ref_out, ref_status, cpu = cpu_baseline(w, host_pool.reshape(-1), host_q, budget_s=args.cpu_budget)
+        # parity on the bytes that were timed: the GPU output of the measured
+        # step against the reference's output for every sequence of the batch
+        gpu_out = out.float().cpu().numpy()
+        tol = 2e-2 if w.dtype == "bf16" else 1e-5 * max(1.0, float(np.abs(ref_out).max()))
+        max_err = float(np.max(np.abs(gpu_out - ref_out)))
+        parity = {"max_abs_err": max_err, "tol": tol, "sequences": int(w.batch),
+                  "against": cpu["kind"], "reference_ok": bool(ref_status.all()),
+                  "pass": bool(max_err <= tol and ref_status.all())}
+
+    if comm is not None:
+        torch.cuda.synchronize()
+        qvp.nccl_comm_destroy(comm)
 
     if rank == 0:
         traffic = NCU_TRAFFIC_BYTES.get(w.name)
+        global_batch = w.batch * dp
+        if sharded:
+            parallelism = (f"kv-head shards x{hp} (each GPU {w.num_kv_heads} kv / {w.num_query_heads} q heads) "
+                           f"x sequence groups x{dp}" +
+                           ("" if args.no_gather else "; per step: decode + NCCL all-gather (libqvp, in place) "
+                                                      "+ reassemble kernel to [B, Hq, D] inside the timed region"))
+        elif world > 1:
+            parallelism = f"sequence groups x{dp} (one batch per GPU, no collective)"
+        else:
+            parallelism = "1 GPU" + (f" (emulating one GPU of a {args.emulate_shards}-way kv-head split, no "
+                                     f"collective)" if args.emulate_shards else "")
         line = {
             "metric": METRIC,
             "value": round(value, 2),
@@ -359,8 +410,7 @@ def run_ours(args):
             "config": {
                 "workload": w.name,
                 "batch_per_gpu": w.batch,
-                "global_batch": w.batch * (world if scaling == "weak" else dp),
-                "cuda_graph": graphed,
+                "global_batch": global_batch,
                 "context_lens": f"{int(w.context_lens.min())}..{int(w.context_lens.max())} "
                                 f"(sum {int(w.context_lens.sum())})",
                 "heads": f"{w.num_query_heads}q/{w.num_kv_heads}kv per GPU",
@@ -370,13 +420,10 @@ def run_ours(args):
                 "split_tokens": plan["split_tokens"],
                 "num_splits_max": plan["num_splits"],
                 "kernel": kernel_name,
-                "combine_threads": args.combine_threads if plan["stream"] else None,
-                "l2": f"inputs larger than L2 ({w.kv_bytes() / 1e6:.0f} MB of K/V read per step)",
-                "parallelism": f"dp{world}" if scaling == "weak" else
-                (f"kv-head shards x{w.meta.get('head_parts', world)} x sequence shards x{w.meta.get('batch_parts', 1)}")
-                + (" + NCCL all-gather of outputs" if world > 1 and not args.no_gather else ""),
+                "l2": f"inputs larger than L2 ({w.kv_bytes() / 1e6:.0f} MB of K/V read per step per GPU)",
+                "parallelism": parallelism,
             },
-            "seqs_per_s": round(w.batch * (world if scaling == "weak" else dp) / (ms_step * 1e-3), 1),
+            "seqs_per_s": round(global_batch / (ms_step * 1e-3), 1),
             "roofline": {
                 "bound": "hbm",
                 "achieved": round(achieved, 1),
@@ -395,7 +442,8 @@ def run_ours(args):
                 "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),
-                "path": "C ABI qvp_decode; per step one H2D of tables+ctx+q from pinned memory and one D2H of "
+                "path": ("C ABI qvp_shard_decode" if comm is not None else "C ABI qvp_decode") +
+                        "; per step one H2D of tables+ctx+q from pinned memory and one D2H of "
                         "out, on two copy streams double-buffered against the decode",
             },
             "gpu_launches": launches_per_step * args.steps,
@@ -403,7 +451,11 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if parity is not None:
+            line["parity"] = parity
         print(json.dumps(line), flush=True)
+        if parity is not None and not parity["pass"]:
+            raise SystemExit(f"parity failure against the reference: {parity}")
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -435,7 +487,7 @@ def cpu_baseline(w, pool, q, budget_s=15.0, threads=None):
     else:
         run = lambda: oracle.port_decode(sub, pool, q[:n], threads=threads)  # noqa: E731
     t0 = time.perf_counter()
-    _, status = run()
+    ref_out, status = run()
     first = time.perf_counter() - t0
     reps = max(1, min(50, int(budget_s / max(first, 1e-6))))
     t0 = time.perf_counter()
@@ -444,7 +496,9 @@ def cpu_baseline(w, pool, q, budget_s=15.0, threads=None):
     dt = (time.perf_counter() - t0) / reps
     if kind == "reference":
         r.close()
-    return {"value": round(sub.algorithmic_bytes() / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
+        if w.dtype == "bf16":
+            ref_out = W.bf16_bits_to_f32(ref_out)
+    return ref_out, status, {"value": round(sub.algorithmic_bytes() / dt / 1e9, 4), "unit": "GB/s", "cores": threads,
             "kind": kind, "ms_per_step": round(dt * 1e3, 3), "seqs_per_s": round(n / dt, 2),
             "sample": f"all {n} sequences of {w.name} (same seeded bytes as the GPU run), "
                       f"{reps} repetitions after 1 untimed, {threads} threads, "
@@ -458,7 +512,7 @@ def run_reference(args):
         return
     import oracle
 
-    w, scaling = make_workload(args.workload, 0, 1, 1)
+    w, scaling, _, _ = make_workload(args.workload, 1)
     pool, q = W.host_inputs(w)
     threads = cpu_threads()
     kind = "reference" if oracle.ref_available() else "port"
@@ -723,18 +777,14 @@ def main():
     p.add_argument("--split", type=int, default=0, help="split-K partition in tokens (0 = auto)")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
-    p.add_argument("--no-gather", action="store_true", help="cfg4 shards: skip the output all-gather")
-    p.add_argument("--graph", action="store_true",
-                   help="multi-GPU cfg4: capture decode + all-gather in a CUDA graph (experimental)")
+    p.add_argument("--no-gather", action="store_true", help="kv-head shards: skip the output all-gather")
+    p.add_argument("--emulate-shards", type=int, choices=[0, 2, 4, 8], default=0,
+                   help="one GPU: run the workload one GPU of an H-way kv-head split holds (profiling)")
     p.add_argument("--shard", choices=["hybrid", "heads"], default="hybrid",
                    help="cfg4 over N GPUs: kv heads only, or kv heads (>= 4 per GPU) then sequences")
-    p.add_argument("--combine-threads", type=int, choices=[64, 128, 256], default=256,
-                   help="CTA size of the stream-K combine (QVP_COMBINE_THREADS)")
     p.add_argument("--profile", action="store_true",
                    help="for ncu: only warm-up and timed decode steps (no clock probe, e2e or CPU baseline)")
     args = p.parse_args()
-    # read by libqvp at its first combine launch
-    os.environ["QVP_COMBINE_THREADS"] = str(args.combine_threads)
     if args.warmup < 3:
         args.warmup = 3
     if args.workload == "prefill" and args.impl == "ours":

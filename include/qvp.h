@@ -177,7 +177,10 @@ QVP_API int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream);
  *   - It calls no cudaMalloc, cudaFree or other allocating routine. The first
  *     call on each device looks up the array's device address
  *     (cudaGetSymbolAddress) with that device current; make that first call
- *     before any stream capture.
+ *     before any stream capture. The address is kept per device ordinal and
+ *     belongs to the device's primary context (the runtime API's context):
+ *     callers that make another context current through the driver API must
+ *     not use this entry point.
  *   - Every call shares the one array, which keeps the last call's contents.
  *     Nothing in it needs to start at zero (the kernels write every scratch
  *     byte they read), but calls that overlap on the GPU (other streams, other
@@ -262,6 +265,66 @@ QVP_API int qvp_kv_append(void* pool, size_t block_stride, uint32_t num_blocks,
                   uint32_t max_blocks_per_seq, const int32_t* block_tables,
                   const int32_t* positions, const void* k, const void* v,
                   int32_t* error_word, qvp_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * KV-head sharding across the GPUs of one node (one process per GPU).
+ *
+ * Each GQA group (a kv head and the num_query_heads/num_kv_heads query heads
+ * that read it) is independent (PagedAttention.h:94-96), so a batch splits by
+ * kv head with no exchange inside the decode: shard s of n owns kv heads
+ * [s*Hkv/n, (s+1)*Hkv/n) and query heads [s*Hq/n, (s+1)*Hq/n). Its pool holds
+ * blocks of num_kv_heads = Hkv/n; the host bookkeeping (allocator, tables,
+ * copy-on-write, swap) is replicated, so every shard uses the same block ids
+ * and tables (the view every shard decodes through is the one
+ * KVCacheManager::cache_view builds, src/KVCacheManager.cpp:241-256). Only
+ * where a consumer needs every head on every GPU are the outputs reassembled:
+ * qvp_shard_decode decodes into its slot of a gather buffer, all-gathers the
+ * slots with NCCL over NVLink (in place, on the caller's communicator and
+ * stream) and reorders them into [batch][Hq][head_dim].
+ *
+ * NCCL is loaded at the first call that needs it (dlopen of libnccl.so.2: the
+ * copy already in the process if there is one), so the rest of the library
+ * does not depend on it. No counterpart in the reference (it runs on one CPU).
+ * ------------------------------------------------------------------------- */
+typedef struct qvp_shard {
+    uint32_t shard;        /* this GPU's shard, in [0, num_shards)            */
+    uint32_t num_shards;   /* GPUs sharing the batch by kv head               */
+    int device;            /* CUDA device of this shard; must be current      */
+} qvp_shard;
+
+typedef struct qvp_shard_decode_args {
+    qvp_shard shard;
+    /* the decode of this shard: its pool (num_kv_heads = Hkv/num_shards), its
+     * queries [batch][Hq/num_shards][head_dim] and num_query_heads =
+     * Hq/num_shards; decode.out is ignored (the output goes to `gathered`). */
+    qvp_decode_args decode;
+    void* nccl_comm;       /* ncclComm_t over the num_shards GPUs, rank = shard */
+    void* gathered;        /* device, qvp_shard_gather_bytes: [num_shards][batch]
+                              [Hq/num_shards][head_dim]                        */
+    void* out;             /* device [batch][Hq][head_dim], every head         */
+} qvp_shard_decode_args;
+
+/* Bytes of the `gathered` buffer qvp_shard_decode needs. */
+QVP_API int qvp_shard_gather_bytes(const qvp_shard_decode_args* args, size_t* bytes);
+/* Decode + in-place NCCL all-gather + reorder, enqueued on `stream`. Every
+ * shard of the communicator must make the matching call (the all-gather is a
+ * collective). The decode's workspace rules are qvp_decode's. */
+QVP_API int qvp_shard_decode(const qvp_shard_decode_args* args, qvp_stream_t stream);
+/* The reorder step alone: gathered [num_shards][batch][heads_per_shard]
+ * [head_dim] -> out [batch][num_shards * heads_per_shard][head_dim]. */
+QVP_API int qvp_shard_reassemble(const void* gathered, void* out, uint32_t num_shards,
+                         uint32_t batch, uint32_t heads_per_shard, uint32_t head_dim,
+                         uint32_t bytes_per_element, qvp_stream_t stream);
+
+/* NCCL communicator helpers for callers that have no NCCL binding of their
+ * own (FFI callers): the unique id (QVP_NCCL_ID_BYTES opaque bytes) is made
+ * on one rank and handed to the others by the caller's own transport. The
+ * communicator belongs to the current device. comm_init blocks until every
+ * rank has joined; comm_destroy waits for the communicator's work. */
+#define QVP_NCCL_ID_BYTES 128
+QVP_API int qvp_nccl_unique_id(void* id, size_t bytes);
+QVP_API int qvp_nccl_comm_init(const void* id, size_t bytes, int nranks, int rank, void** comm);
+QVP_API int qvp_nccl_comm_destroy(void* comm);
 
 #ifdef __cplusplus
 }

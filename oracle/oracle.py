@@ -58,7 +58,7 @@ def ref_lib() -> C.CDLL:
     global _ref
     if _ref is None:
         if not os.path.exists(REF_PATH):
-            raise ImportError(f"{REF_PATH} missing; build it with `make -C oracle` where the reference exists")
+            raise ImportError(f"{REF_PATH} missing; build it with `make -C oracle REF=<reference checkout>`")
         lib = C.CDLL(REF_PATH)
         vp, u32 = C.c_void_p, C.c_uint32
         lib.ref_pool_create.restype = vp

@@ -30,7 +30,6 @@
 #include <cudaTypedefs.h>
 
 #include <cmath>
-#include <cstdlib>
 #include <cstring>
 
 namespace qvp {
@@ -656,9 +655,8 @@ constexpr int kFewParts = 16;  // partials merged by the one-round-trip path
 // Merges the stream-K records of each (segment, kv head) into the output:
 // grid.x = nseg * HH, THREADS threads. Launched as a programmatic dependent of
 // paged_decode_stream; it waits for that grid (griddepcontrol.wait) before
-// reading anything. THREADS (256 by default; 64 or 128 with
-// QVP_COMBINE_THREADS) sets the CTA size: smaller CTAs fit more of the grid
-// into one wave. The warps split the segment's partial records
+// reading anything. THREADS is the CTA size (256: measured faster on cfg2
+// than 64 or 128, which fit more of the grid into one wave). The warps split the segment's partial records
 // (warp w takes partials w, w + warps, ...) when there are more than
 // kFewParts of them; each lane keeps its share of the
 // G x D outputs in registers and issues all of a partial's loads at once;
@@ -1091,17 +1089,6 @@ int launch_fast(const qvp_decode_args& a, const DecodePlan& plan, const FastPara
     }
 }
 
-// CTA size of the combine: kCombineThreads unless QVP_COMBINE_THREADS is 64
-// or 128 (read once per process).
-int combine_threads() {
-    static const int threads = [] {
-        const char* v = std::getenv("QVP_COMBINE_THREADS");
-        const int n = v != nullptr ? std::atoi(v) : 0;
-        return (n == 64 || n == 128) ? n : kCombineThreads;
-    }();
-    return threads;
-}
-
 // The combine is a programmatic dependent: it may be scheduled while the
 // decode grid still runs and waits (griddepcontrol.wait) for its results.
 template <int D, int HH, int J, int THREADS>
@@ -1162,11 +1149,7 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
         if (rc != QVP_OK) return rc;
     }
 
-    switch (combine_threads()) {
-        case 64: return launch_combine<D, HH, J, 64>(a, plan, sp, st);
-        case 128: return launch_combine<D, HH, J, 128>(a, plan, sp, st);
-        default: return launch_combine<D, HH, J, kCombineThreads>(a, plan, sp, st);
-    }
+    return launch_combine<D, HH, J, kCombineThreads>(a, plan, sp, st);
 }
 
 int launch_stream(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
@@ -1289,17 +1272,20 @@ extern "C" int qvp_decode_plan(const qvp_decode_args* args, uint32_t* split_toke
 
 extern "C" int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream) {
     if (args == nullptr) return fail(QVP_ERR_INVALID, "null argument");
-    const qvp_decode_args& a = *args;
     DecodePlan plan;
-    int rc = plan_decode(a, plan);
-    if (rc != QVP_OK || a.batch == 0) return rc;
+    const int rc = plan_decode(*args, plan);
+    if (rc != QVP_OK || args->batch == 0) return rc;
+    return run_decode(*args, plan, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int qvp::run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream_t st) {
+    int rc = QVP_OK;
     if (plan.workspace_bytes > 0 && (a.workspace == nullptr || a.workspace_bytes < plan.workspace_bytes))
         return fail(QVP_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", plan.workspace_bytes,
                     a.workspace == nullptr ? size_t(0) : a.workspace_bytes);
     // partial records are read back as float4
     if (plan.workspace_bytes > 0 && (reinterpret_cast<uintptr_t>(a.workspace) & 15u) != 0)
         return fail(QVP_ERR_WORKSPACE, "workspace is not 16-byte aligned");
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const size_t parts = static_cast<size_t>(a.batch) * plan.max_splits * a.num_query_heads;
     float* ws_o = static_cast<float*>(a.workspace);
     float2* ws_ml = plan.workspace_bytes

@@ -11,6 +11,8 @@
 // queries and output; only the split-K / stream-K scratch comes from here.
 #include "qvp_internal.h"
 
+#include <atomic>
+
 namespace {
 
 // 16 MiB of device memory, held by every GPU that loads the library until
@@ -22,9 +24,12 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 // Device address of g_noalloc_scratch per device ordinal, looked up once
 // with that device current. In host code the symbol itself is only a
-// host-side stand-in, never a device address.
+// host-side stand-in, never a device address. The address belongs to the
+// device's primary context (the one the runtime API makes current). Threads
+// making their first call on a device at the same time both look it up and
+// store the same pointer; the atomic makes that race well defined.
 constexpr int kMaxDevices = 64;
-void* g_scratch_addr[kMaxDevices] = {};
+std::atomic<void*> g_scratch_addr[kMaxDevices] = {};
 
 }  // namespace
 
@@ -32,9 +37,10 @@ using namespace qvp;
 
 extern "C" int qvp_decode_noalloc(const qvp_decode_args* args, qvp_stream_t stream) {
     if (args == nullptr) return fail(QVP_ERR_INVALID, "null argument");
-    size_t need = 0;
-    int rc = qvp_decode_workspace_size(args, &need);
-    if (rc != QVP_OK) return rc;
+    DecodePlan plan;
+    int rc = plan_decode(*args, plan);
+    if (rc != QVP_OK || args->batch == 0) return rc;
+    const size_t need = plan.workspace_bytes;
     if (need > kNoAllocScratchBytes)
         return fail(QVP_ERR_WORKSPACE,
                     "qvp_decode_noalloc: this batch needs %zu bytes of scratch but the static array holds %zu; "
@@ -44,14 +50,14 @@ extern "C" int qvp_decode_noalloc(const qvp_decode_args* args, qvp_stream_t stre
     rc = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
     if (rc != QVP_OK) return rc;
     if (dev < 0 || dev >= kMaxDevices) return fail(QVP_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
-    if (g_scratch_addr[dev] == nullptr) {
-        void* ptr = nullptr;
-        rc = check_cuda(cudaGetSymbolAddress(&ptr, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
+    void* scratch = g_scratch_addr[dev].load(std::memory_order_relaxed);
+    if (scratch == nullptr) {
+        rc = check_cuda(cudaGetSymbolAddress(&scratch, g_noalloc_scratch), "cudaGetSymbolAddress(no-alloc scratch)");
         if (rc != QVP_OK) return rc;
-        g_scratch_addr[dev] = ptr;
+        g_scratch_addr[dev].store(scratch, std::memory_order_relaxed);
     }
     qvp_decode_args a = *args;
-    a.workspace = g_scratch_addr[dev];
+    a.workspace = scratch;
     a.workspace_bytes = kNoAllocScratchBytes;
-    return qvp_decode(&a, stream);
+    return run_decode(a, plan, reinterpret_cast<cudaStream_t>(stream));
 }

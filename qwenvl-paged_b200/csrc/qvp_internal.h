@@ -44,6 +44,9 @@ struct DecodePlan {
 
 // Validates `a` and fills `plan`; returns a qvp_status.
 int plan_decode(const qvp_decode_args& a, DecodePlan& plan);
+// Launches the decode `plan` (from plan_decode on the same arguments, batch
+// > 0) after checking the caller's workspace against it.
+int run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream_t st);
 
 int device_sm_count();
 

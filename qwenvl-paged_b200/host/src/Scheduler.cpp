@@ -39,7 +39,7 @@ BatchPlan Scheduler::schedule_next() {
         reclaim_for_admission(next.prompt_tokens, plan.prefill_requests.size());
         if (!cache_manager_->create_sequence(sequence_metadata(next))) break;
         if (!cache_manager_->reserve_tokens(next.root_sequence_id, next.prompt_tokens)) {
-            // leave no state behind; a later step may admit it
+            // reference src/Scheduler.cpp:53-56
             cache_manager_->release_sequence(next.root_sequence_id);
             break;
         }
@@ -124,16 +124,15 @@ void Scheduler::reclaim_for_admission(std::uint32_t prompt_tokens, std::size_t a
     if (config_.preemption_watermark_blocks == 0) return;
     const AllocatorStats st = allocator_->stats();
     const std::uint32_t need = blocks_for_tokens(prompt_tokens);
-    // a prompt larger than the pool can never fit; do not evict for it
+    // reference src/Scheduler.cpp:180-185
     if (need == 0 || need > st.total_blocks) return;
     const std::uint32_t target = std::min(need + config_.preemption_watermark_blocks, st.total_blocks);
     while (active_.size() > admitted_this_step && allocator_->stats().free_blocks < target) {
         const std::uint32_t free_before = allocator_->stats().free_blocks;
-        // newest request that predates this call (the ones admitted by this
-        // call sit at the back of the queue)
+        // victim order: reference src/Scheduler.cpp:196-199
         const RequestId victim = active_[active_.size() - admitted_this_step - 1].request_id;
         if (!preempt(victim, "cache pressure watermark")) break;
-        if (allocator_->stats().free_blocks <= free_before) break;  // nothing reclaimed (no swap backend)
+        if (allocator_->stats().free_blocks <= free_before) break;  // reference src/Scheduler.cpp:203-207
     }
 }
 

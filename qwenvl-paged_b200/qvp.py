@@ -98,6 +98,23 @@ class PrefillArgs(C.Structure):
     ]
 
 
+class Shard(C.Structure):
+    _fields_ = [("shard", C.c_uint32), ("num_shards", C.c_uint32), ("device", C.c_int)]
+
+
+class ShardDecodeArgs(C.Structure):
+    _fields_ = [
+        ("shard", Shard),
+        ("decode", DecodeArgs),
+        ("nccl_comm", C.c_void_p),
+        ("gathered", C.c_void_p),
+        ("out", C.c_void_p),
+    ]
+
+
+NCCL_ID_BYTES = 128
+
+
 def _load() -> C.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
@@ -128,6 +145,12 @@ def _load() -> C.CDLL:
         "qvp_gather_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
         "qvp_scatter_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
         "qvp_kv_append": (C.c_int, [vp, sz, u32, P(BlockShape), u32, u32, u32, vp, vp, vp, vp, vp, vp]),
+        "qvp_shard_gather_bytes": (C.c_int, [P(ShardDecodeArgs), P(sz)]),
+        "qvp_shard_decode": (C.c_int, [P(ShardDecodeArgs), vp]),
+        "qvp_shard_reassemble": (C.c_int, [vp, vp, u32, u32, u32, u32, u32, vp]),
+        "qvp_nccl_unique_id": (C.c_int, [vp, sz]),
+        "qvp_nccl_comm_init": (C.c_int, [vp, sz, C.c_int, C.c_int, P(vp)]),
+        "qvp_nccl_comm_destroy": (C.c_int, [vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -145,7 +168,8 @@ EXPORTED = [
     "qvp_pool_create", "qvp_pool_destroy", "qvp_pool_base", "qvp_pool_stride", "qvp_pool_num_blocks",
     "qvp_pool_device", "qvp_pool_write", "qvp_pool_read", "qvp_decode_workspace_size",
     "qvp_decode_plan", "qvp_decode", "qvp_decode_noalloc", "qvp_prefill", "qvp_copy_blocks", "qvp_gather_blocks", "qvp_scatter_blocks",
-    "qvp_kv_append",
+    "qvp_kv_append", "qvp_shard_gather_bytes", "qvp_shard_decode", "qvp_shard_reassemble",
+    "qvp_nccl_unique_id", "qvp_nccl_comm_init", "qvp_nccl_comm_destroy",
 ]
 
 
@@ -224,3 +248,32 @@ def decode_plan(args: DecodeArgs):
 def decode(args: DecodeArgs, stream: int = 0) -> int:
     """Enqueues one batched decode; returns the status (does not raise)."""
     return lib.qvp_decode(C.byref(args), stream or None)
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (make it on one rank, hand it to the others)."""
+    buf = (C.c_char * NCCL_ID_BYTES)()
+    check(lib.qvp_nccl_unique_id(buf, NCCL_ID_BYTES), "qvp_nccl_unique_id")
+    return bytes(buf)
+
+
+def nccl_comm_init(uid: bytes, nranks: int, rank: int) -> int:
+    """An NCCL communicator on the current device (blocks until all join)."""
+    buf = (C.c_char * len(uid)).from_buffer_copy(uid)
+    comm = C.c_void_p()
+    check(lib.qvp_nccl_comm_init(buf, len(uid), nranks, rank, C.byref(comm)), "qvp_nccl_comm_init")
+    return comm.value
+
+
+def nccl_comm_destroy(comm: int) -> None:
+    check(lib.qvp_nccl_comm_destroy(comm), "qvp_nccl_comm_destroy")
+
+
+def shard_decode_args(decode: DecodeArgs, shard: int, num_shards: int, device: int, comm, gathered, out):
+    return ShardDecodeArgs(Shard(shard, num_shards, device), decode, comm or None, gathered, out)
+
+
+def shard_gather_bytes(args: ShardDecodeArgs) -> int:
+    n = C.c_size_t()
+    check(lib.qvp_shard_gather_bytes(C.byref(args), C.byref(n)), "qvp_shard_gather_bytes")
+    return n.value

@@ -122,6 +122,23 @@ def cfg2(seed: int = 2, batch: int = 64, lo: int = 512, hi: int = 8192) -> Decod
                           num_blocks, seed)
 
 
+def cfg2_shard(head_parts: int = 1, seed: int = 2) -> DecodeWorkload:
+    """What one GPU holds when the 7B-shaped decode is split by kv head over
+    `head_parts` GPUs at constant bytes per GPU: a batch of 64*head_parts
+    sequences (ctx ~ U[512, 8192], seeded), of which this GPU owns
+    4/head_parts kv heads and their 28/head_parts query heads. head_parts = 1
+    is cfg2 itself."""
+    if head_parts not in (1, 2, 4):
+        raise ValueError(f"cfg2 has 4 kv heads; cannot split them {head_parts} ways")
+    w = cfg2(seed=seed, batch=64 * head_parts)
+    if head_parts > 1:
+        w.num_kv_heads //= head_parts
+        w.num_query_heads //= head_parts
+        w.name = f"cfg2-qwen2vl-7b-decode-kvshard{head_parts}"
+    w.meta = {"head_parts": head_parts}
+    return w
+
+
 def cfg4(seed: int = 4, batch: int = 32, ctx_len: int = 32768, shards: int = 1) -> DecodeWorkload:
     """One kv-head shard of the 72B-shaped config (8 // shards kv heads)."""
     assert 8 % shards == 0

@@ -6,7 +6,7 @@ into oracle/_ref/libqvp_ref.so by oracle/Makefile) on the seeded workloads of
 qwenvl-paged_b200/workloads.py and stores the outputs with a hash of the
 inputs they were computed from. Usage (where the reference sources exist):
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle REF=<reference checkout> && python tests/golden/make_golden.py
 """
 import hashlib
 import json

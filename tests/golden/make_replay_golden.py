@@ -1,7 +1,7 @@
 """Regenerates tests/golden/replay_golden.json: the sha256 of the trace the
 reference's own classes (oracle/_ref/libqvp_ref.so, built from the reference
 sources by oracle/Makefile) produce for every bookkeeping script of
-tests/replay_scripts.py. Usage: make -C oracle && python tests/golden/make_replay_golden.py
+tests/replay_scripts.py. Usage: make -C oracle REF=<reference checkout> && python tests/golden/make_replay_golden.py
 """
 import json
 import os

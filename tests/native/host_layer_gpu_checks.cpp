@@ -1,5 +1,5 @@
 // TEST INFRASTRUCTURE: GPU checks of the host layer's additions on device
-// pools, driven by tests/host_layer_gpu_checks.py:
+// pools, driven by tests/test_host_layer_gpu.py:
 //  * PagedDecodeBatch with device-resident block tables against the per-step
 //    flatten: over decode steps that cross block boundaries, copy on write,
 //    reorder the batch and refuse a swapped-out sequence, both must write

@@ -3,11 +3,7 @@ PagedDecodeBatch with device-resident block tables (bit-identical outputs to
 the per-step flatten across block growth, copy on write, reordering and a
 refused swapped-out sequence, no table rows uploaded on steady steps),
 KVAppendBatch (appended K/V land byte-exact in their slots) and
-PagedPrefillBatch (within the bf16 tolerance of per-position decodes).
-
-Not collected yet (no test_ prefix): run it on a GPU with
-`python -m pytest tests/host_layer_gpu_checks.py -q`, then rename it to
-test_host_layer_gpu.py."""
+PagedPrefillBatch (within the bf16 tolerance of per-position decodes)."""
 import os
 
 import pytest

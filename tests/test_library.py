@@ -115,3 +115,19 @@ def test_movers_reject_bad_arguments():
     assert lib.qvp_kv_append(None, 256, 4, C.byref(s), 0, 1, 1, None, None, None, None, None, None) == qvp.ERR_INVALID
     assert lib.qvp_kv_append(C.c_void_p(1), 256, 4, C.byref(s), 1, 1, 1, C.c_void_p(1), C.c_void_p(1),
                              C.c_void_p(1), C.c_void_p(1), None, None) == qvp.ERR_INVALID
+
+
+def test_shard_gather_bytes_and_refusals_on_the_host():
+    a = _args(shape=qvp.make_shape(16, 1, 1, 128, 2), dtype=qvp.DTYPE_BF16, block_stride=8192,
+              num_query_heads=7, batch=64, max_blocks_per_seq=4, max_context_len=64)
+    sa = qvp.shard_decode_args(a, 1, 4, -1, None, 0, 0)
+    # four slots of [64][7][128] bf16
+    assert qvp.shard_gather_bytes(sa) == 4 * 64 * 7 * 128 * 2
+    n = C.c_size_t()
+    bad = qvp.shard_decode_args(a, 4, 4, -1, None, 0, 0)
+    assert qvp.lib.qvp_shard_gather_bytes(C.byref(bad), C.byref(n)) == qvp.ERR_INVALID
+    assert qvp.lib.qvp_shard_reassemble(None, None, 0, 1, 1, 1, 2, None) == qvp.ERR_INVALID
+    # nothing to move: no launch, no error
+    assert qvp.lib.qvp_shard_reassemble(None, None, 2, 0, 7, 128, 2, None) == qvp.OK
+    assert qvp.lib.qvp_nccl_comm_init(None, 0, 2, 0, C.byref(C.c_void_p())) == qvp.ERR_INVALID
+    assert qvp.lib.qvp_nccl_comm_destroy(None) == qvp.OK

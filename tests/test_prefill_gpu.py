@@ -1,11 +1,5 @@
 """GPU parity checks of qvp_prefill against the prefill oracle (the
-reference's decode at every prompt position).
-
-Not collected by pytest yet (the file name does not start with test_): the
-prefill kernels compile but have not run on a B200. Run it explicitly with
-`python -m pytest tests/prefill_gpu_checks.py` on a GPU box; once green it
-becomes tests/test_prefill_gpu.py.
-"""
+reference's decode at every prompt position)."""
 import numpy as np
 import pytest
 

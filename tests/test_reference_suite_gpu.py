@@ -1,12 +1,9 @@
 """The reference's nine test files, unmodified, against libqvp.so on a GPU
 with host-visible pools (QVP_HOST_VISIBLE_POOLS=1, CUDA managed memory), so
 that the cases which write and read block bytes through PhysicalBlock::data()
-and CacheView::slot<T>() run too: all 131 cases must pass.
-
-Not collected yet (no test_ prefix): host-visible pools have not run on a
-GPU. Run `python -m pytest tests/reference_suite_gpu_checks.py -q` on a GPU
-box, then rename it to test_reference_suite_gpu.py. The binaries are built by
-oracle/Makefile where the reference sources are present and travel prebuilt."""
+and CacheView::slot<T>() run too: all 131 cases must pass. The binaries are
+built by oracle/Makefile where the reference sources are present and travel
+prebuilt."""
 import glob
 import os
 import re

@@ -2,8 +2,8 @@
 cannot allocate device memory (a host that owns the whole HBM budget, an FFI
 caller with no device allocator, a step loop where cudaMalloc would
 synchronise the device). Its scratch is a fixed 16 MiB array inside the
-library; it must give the same outputs as qvp_decode with a caller
-workspace, call after call, and refuse batches whose scratch would not fit.
+library; it must give outputs identical (bit for bit) to qvp_decode with a caller
+workspace, call after call, whatever the array held before, and refuse batches whose scratch would not fit.
 
 Named test_zz_* so pytest collects it last.
 """
@@ -18,8 +18,6 @@ from helpers import gpu_decode
 
 pytestmark = pytest.mark.gpu
 
-BF16_ABS = 2e-2   # the bf16 tolerance of the decode parity tests
-F32_REL = 1e-5    # the fp32 tolerance of the decode parity tests
 STATIC_SCRATCH = 16 << 20
 
 
@@ -46,15 +44,22 @@ def _device_args(w, pool, q, split_tokens=0):
     return a, bufs
 
 
-@pytest.mark.parametrize("case", ["bf16-stream-k", "bf16-grid-split", "fp32-generic-split"])
-def test_no_alloc_decode_matches_qvp_decode_on_two_calls_in_a_row(case):
+def _case(name):
+    if name == "bf16-stream-k":
+        return W.small(31, batch=16, ctx_lo=1, ctx_hi=3000, hq=28, hkv=4, head_dim=128, dtype="bf16"), 0
+    if name == "bf16-stream-k-large":
+        return W.small(34, batch=96, ctx_lo=500, ctx_hi=6000, hq=28, hkv=4, head_dim=128, dtype="bf16"), 0
+    if name == "bf16-grid-split":
+        return W.small(32, batch=8, ctx_lo=100, ctx_hi=2500, hq=28, hkv=4, head_dim=128, dtype="bf16"), 256
+    return W.cfg1(), 48
+
+
+def _check_calls(name, calls=2):
+    """Runs `name` through qvp_decode (caller workspace) once and through
+    qvp_decode_noalloc `calls` times; the kernels and the plan are the same,
+    so the outputs must be identical bit for bit."""
     import torch
-    if case == "bf16-stream-k":
-        w, split = W.small(31, batch=16, ctx_lo=1, ctx_hi=3000, hq=28, hkv=4, head_dim=128, dtype="bf16"), 0
-    elif case == "bf16-grid-split":
-        w, split = W.small(32, batch=8, ctx_lo=100, ctx_hi=2500, hq=28, hkv=4, head_dim=128, dtype="bf16"), 256
-    else:
-        w, split = W.cfg1(), 48
+    w, split = _case(name)
     pool, q = W.host_inputs(w)
     st, want, err, plan = gpu_decode(w, pool, q, split_tokens=split)   # caller-workspace entry point
     assert st == 0 and err == 0
@@ -62,16 +67,27 @@ def test_no_alloc_decode_matches_qvp_decode_on_two_calls_in_a_row(case):
 
     a, bufs = _device_args(w, pool, q, split)
     stream = torch.cuda.current_stream().cuda_stream
-    for call in range(2):
+    for call in range(calls):
         bufs["out"].fill_(-7.0)
         assert qvp.lib.qvp_decode_noalloc(C.byref(a), stream) == 0, qvp.last_error()
         torch.cuda.synchronize()
         got = bufs["out"].float().cpu().numpy()
         assert int(bufs["err"].item()) == 0
-        if w.dtype == "bf16":
-            assert np.max(np.abs(got - want)) <= BF16_ABS, call
-        else:
-            assert np.max(np.abs(got - want)) <= F32_REL * max(1.0, float(np.abs(want).max())), call
+        assert np.array_equal(got, want), (name, call, float(np.max(np.abs(got - want))))
+    return plan["workspace_bytes"]
+
+
+@pytest.mark.parametrize("case", ["bf16-stream-k", "bf16-grid-split", "fp32-generic-split"])
+def test_no_alloc_decode_matches_qvp_decode_on_two_calls_in_a_row(case):
+    _check_calls(case)
+
+
+def test_no_alloc_decode_after_a_larger_call_ignores_stale_scratch():
+    # the larger batch leaves records all over the shared array; the smaller
+    # one that follows must not read any of them
+    big = _check_calls("bf16-stream-k-large", calls=1)
+    small = _check_calls("bf16-stream-k", calls=2)
+    assert big > small
 
 
 def test_no_alloc_decode_refuses_batches_beyond_its_scratch():
