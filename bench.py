@@ -198,8 +198,9 @@ def run_ours(args):
         a.workspace_bytes = plan["workspace_bytes"]
     stream = torch.cuda.current_stream()
     sh = stream.cuda_stream
-    launches_per_step = 2 if plan["stream"] else 1 + (1 if plan["num_splits"] > 1 else 0)
-    kernel_name = ("paged_decode_stream (persistent stream-K, TMA + mma.sync) + combine_records" if plan["stream"]
+    launches_per_step = 1 if plan["stream"] else 1 + (1 if plan["num_splits"] > 1 else 0)
+    kernel_name = ("paged_decode_stream (persistent stream-K, TMA + mma.sync, in-kernel merge of split segments)"
+                   if plan["stream"]
                    else "paged_decode_fast (grid split-K, TMA + mma.sync) + combine_partitions" if plan["fast"]
                    else "paged_decode_generic + combine_partitions")
 

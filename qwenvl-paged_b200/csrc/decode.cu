@@ -7,11 +7,17 @@
 // with fp32 accumulation. The reference takes an exact max and then sums
 // exp(s - max) (PagedAttention.h:98-118); here each partition keeps a running
 // (max, sum, accumulator) and rescales when the max grows, which is the same
-// value in exact arithmetic. Partitions of long contexts (split-K) are merged
-// by `combine_partitions`.
+// value in exact arithmetic.
 //
-// Two kernels:
-//  * paged_decode_fast: bf16 K/V/Q, 16-token blocks, head_dim 64 or 128,
+// Three kernels:
+//  * paged_decode_stream (the default for bf16): the persistent stream-K form
+//    of paged_decode_fast below, one CTA per SM over an even share of all
+//    (sequence, head group, stage) work; the CTA that completes a segment
+//    merges its partial records into the output.
+//  * paged_decode_fast: the same tiles as a grid (sequence, partition, head
+//    group), partitions merged by `combine_partitions`; used when a
+//    partition size is given or a batch has more than 2048 segments.
+//    bf16 K/V/Q, 16-token blocks, head_dim 64 or 128,
 //    at most 16 query heads per kv head, unpadded blocks. One CTA owns
 //    (sequence, partition, group of HH kv heads). A producer warp streams each
 //    block's K and V slices for the CTA's heads into shared memory with TMA
@@ -29,6 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <chrono>
 #include <cmath>
 #include <cstring>
 
@@ -63,8 +70,7 @@ struct FastParams {
 template <int D, int HH, int STAGES>
 struct FastShape {
     static constexpr int J = kFastComputeWarps / HH;     // blocks in flight per stage
-    static constexpr uint32_t kBox = HH * 16 * D * 2;   // one stream of one block, HH heads
-    static constexpr uint32_t kBlock = 2 * kBox;        // K and V
+    static constexpr uint32_t kBlock = 2 * HH * 16 * D * 2;  // K and V of one block, HH heads (one TMA box)
     static constexpr uint32_t kStage = J * kBlock;
     static constexpr uint32_t kSmem = STAGES * kStage + 1024 + 2 * STAGES * 8 + 16;
 };
@@ -89,12 +95,13 @@ __device__ __forceinline__ void load_query_fragments(uint32_t (&qa)[D / 16][4], 
 }
 
 // One 16-token block of one kv head: S = Q K^T on tensor cores, masked to the
-// `valid` leading tokens, online-softmax update, O += P V. `kb` and `vb` are
-// the shared-memory boxes of K and V holding HH heads; `row_head` picks the
-// head inside them.
+// `valid` leading tokens, online-softmax update, O += P V. `blk` is the
+// shared-memory box of the block, [head_dim/64][HH][K 16 | V 16 tokens][64]
+// (one TMA copy), so the K rows of (dh, head) are row group 2*(dh*HH+head)
+// and its V rows the next one; `row_head` picks the head.
 template <int D, int HH>
-__device__ __forceinline__ void attend_block(WarpState<D>& st, const uint32_t (&qa)[D / 16][4], uint32_t kb,
-                                             uint32_t vb, int row_head, int valid, float scale_log2, int lane) {
+__device__ __forceinline__ void attend_block(WarpState<D>& st, const uint32_t (&qa)[D / 16][4], uint32_t blk,
+                                             int row_head, int valid, float scale_log2, int lane) {
     const int c = lane & 3;
     const int mi = lane >> 3;
     const int li = lane & 7;
@@ -107,7 +114,7 @@ __device__ __forceinline__ void attend_block(WarpState<D>& st, const uint32_t (&
         const int chunk = ((ks & 3) << 1) + (mi & 1);
         const int t = ((mi >> 1) << 3) + li;
         uint32_t r0, r1, r2, r3;
-        ldmatrix_x4(box_addr(kb, dh * HH + row_head, t, chunk), r0, r1, r2, r3);
+        ldmatrix_x4(box_addr(blk, (dh * HH + row_head) * 2, t, chunk), r0, r1, r2, r3);
         mma_bf16_16816(s[0], qa[ks], r0, r1);
         mma_bf16_16816(s[1], qa[ks], r2, r3);
     }
@@ -157,7 +164,7 @@ __device__ __forceinline__ void attend_block(WarpState<D>& st, const uint32_t (&
         const int chunk = ((np & 3) << 1) + (mi >> 1);
         const int t = ((mi & 1) << 3) + li;
         uint32_t v0, v1, v2, v3;
-        ldmatrix_x4_trans(box_addr(vb, dh * HH + row_head, t, chunk), v0, v1, v2, v3);
+        ldmatrix_x4_trans(box_addr(blk, (dh * HH + row_head) * 2 + 1, t, chunk), v0, v1, v2, v3);
         if (valid < 16) {
             // V slots past the context may hold anything (even NaN); zero them
             // so the zero weights cannot turn them into NaN.
@@ -242,8 +249,6 @@ __global__ void __launch_bounds__(kFastThreads, 1)
                     }
                     const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
                     tma_load_4d(dst + j * S::kBlock, &tmap, full0 + 8 * slot, 0, r, hg * HH, 0, policy);
-                    tma_load_4d(dst + j * S::kBlock + S::kBox, &tmap, full0 + 8 * slot, 0, r + 16,
-                                hg * HH, 0, policy);
                 }
             }
         }
@@ -275,7 +280,7 @@ __global__ void __launch_bounds__(kFastThreads, 1)
         if (lb < b1) {
             const int valid = min(16, ctx - static_cast<int>(lb) * 16);
             const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
-            attend_block<D, HH>(st, qa, kb, kb + S::kBox, hh, valid, p.scale_log2, lane);
+            attend_block<D, HH>(st, qa, kb, hh, valid, p.scale_log2, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * slot);
@@ -378,10 +383,17 @@ __global__ void __launch_bounds__(kFastThreads, 1)
 // accumulator) per segment piece and writes it as a partial record when the
 // piece ends. Records of segment sigma written by CTA c live at index
 // sigma + c, which is injective because segments and CTA ranges are both
-// contiguous in stage order. `combine_records`, launched as a programmatic
-// dependent (already resident when the decode grid drains), merges them.
+// contiguous in stage order. The CTA that completes the last piece of a
+// segment merges its records into the output (merge_segment): every CTA
+// counts its finished pieces on a per-segment arrival counter, and the one
+// whose arrival completes the count merges the segment once its own stream
+// is done (so the merge never stalls the pipeline). No CTA ever waits for
+// another, so the kernel needs no co-resident grid. The counters live in the
+// workspace, which may hold anything on entry: each holds (epoch << 32 |
+// count), and a word from another epoch (another call) counts as zero.
 
-constexpr int kStreamMaxSegments = 4096;
+constexpr int kStreamMaxSegments = 2048;
+
 
 struct StreamParams {
     const int32_t* tables;
@@ -389,7 +401,8 @@ struct StreamParams {
     const __nv_bfloat16* q;
     float* rec_acc;       // [records][G][D]
     float2* rec_ml;       // [records][G]
-    int32_t* seg_prefix;  // [nseg + 1] stage prefix, written by CTA 0 for the combine
+    unsigned long long* seg_count;  // [nseg] arrival counters (epoch << 32 | pieces)
+    __nv_bfloat16* out;   // [batch][hq][D]
     int32_t* err;
     uint32_t pitch;
     uint32_t num_blocks;
@@ -399,6 +412,7 @@ struct StreamParams {
     uint32_t group;
     uint32_t head_groups;  // z = kv heads / HH
     uint32_t nseg;         // batch * z
+    uint32_t epoch;        // differs between calls
     float scale_log2;
 };
 
@@ -427,6 +441,173 @@ __device__ __forceinline__ int find_segment(const int32_t* prefix, int nseg, uin
             hi = mid - 1;
     }
     return lo;
+}
+
+// First and last CTA whose stage ranges intersect stages [ps, pe) (pe > ps)
+// of a `grid`-CTA stream-K launch over `total` stages: CTA c owns stages
+// [c*total/grid, (c+1)*total/grid).
+__device__ __forceinline__ void pieces_of(uint32_t ps, uint32_t pe, uint32_t total, uint32_t grid, uint32_t& cf,
+                                          uint32_t& cl) {
+    cf = static_cast<uint32_t>((static_cast<uint64_t>(ps + 1) * grid - 1) / total);
+    cl = static_cast<uint32_t>((static_cast<uint64_t>(pe) * grid - 1) / total);
+}
+
+// Counts one finished piece of a segment on its arrival counter; true for the
+// arrival that completes `expected`. A word whose epoch is not `epoch` (left
+// by another call, or never written) counts as zero pieces.
+__device__ __forceinline__ bool arrive_last(unsigned long long* counter, uint32_t epoch, uint32_t expected) {
+    unsigned long long old = *reinterpret_cast<volatile unsigned long long*>(counter);
+    uint32_t done;
+    while (true) {
+        const uint32_t prev = (static_cast<uint32_t>(old >> 32) == epoch) ? static_cast<uint32_t>(old) : 0u;
+        done = prev + 1u;
+        const unsigned long long want = (static_cast<unsigned long long>(epoch) << 32) | done;
+        const unsigned long long seen = atomicCAS(counter, old, want);
+        if (seen == old) break;
+        old = seen;
+    }
+    return done == expected;
+}
+
+// Merges every partial record of segment `sg` (its HH kv heads, G query rows
+// each) into the output; run after the CTA's stream by its kFastComputeWarps
+// consumer warps (tid < 256), with the pipeline's shared memory free. The
+// records of one CTA's piece are contiguous (HH * J of them), so thread 0
+// brings each piece into shared memory with two bulk copies (accumulators,
+// then maxima and sums); as many pieces as fit go in one round trip. Per
+// chunk of pieces: the running max and sum of every row (threads r < HH*G),
+// then each thread rescales its OPT float4 outputs and adds the chunk's parts
+// from shared memory. The order of summation depends on neither the CTA that
+// merges nor timing, so results are identical from call to call.
+template <int D, int HH, int J, int OPT>
+__device__ __forceinline__ bool merge_segment(const float* __restrict__ rec_acc, const float2* __restrict__ rec_ml,
+                                              __nv_bfloat16* __restrict__ out, uint32_t group, uint32_t head_groups,
+                                              uint32_t hq, int sg, uint32_t cf, uint32_t cl, uint32_t total,
+                                              uint32_t grid, uint8_t* stage, uint32_t stage_bytes, uint32_t bar,
+                                              uint32_t& phase, float* s_stat, int tid, int32_t* err) {
+    constexpr int D4 = D / 4;
+    constexpr int kThreads = kFastComputeWarps * 32;
+    constexpr int kParts = HH * J;  // records per piece
+    const int G = static_cast<int>(group);
+    const int R = HH * G;
+    const uint32_t acc_bytes = static_cast<uint32_t>(kParts * G * D) * 4u;
+    const uint32_t ml_bytes = static_cast<uint32_t>(kParts * G) * 8u;
+    const uint32_t piece_bytes = acc_bytes + ml_bytes;
+    const uint32_t per_chunk = stage_bytes / piece_bytes;  // >= 1 for every supported shape
+    float* s_max = s_stat;       // [R] running max
+    float* s_sum = s_stat + 64;  // [R] running sum
+    float* s_scale = s_stat + 128;  // [R] rescale of the running accumulators
+    if (tid < R) {
+        s_max[tid] = -INFINITY;
+        s_sum[tid] = 0.f;
+    }
+    if (tid == 0) s_stat[192] = 0.f;  // wait-timeout vote
+    named_barrier(1, kThreads);
+    const int nout = R * D4;
+    float4 acc[OPT];
+#pragma unroll
+    for (int i = 0; i < OPT; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    uint32_t c = cf;
+    while (c <= cl) {
+        // this chunk: the next per_chunk non-empty CTAs of [c, cl]
+        uint32_t pieces[8];
+        uint32_t np = 0;
+        for (; c <= cl && np < per_chunk && np < 8; ++c)
+            if (!(total < grid && cta_is_empty(c, total, grid))) pieces[np++] = c;
+        if (np == 0) break;
+        if (tid == 0) {
+            // generic-proxy reads of this shared memory are done (barrier
+            // below) and the records were published to this thread (acquire)
+            asm volatile("fence.proxy.async;" ::: "memory");
+            mbar_arrive_expect_tx(bar, np * piece_bytes);
+            for (uint32_t i = 0; i < np; ++i) {
+                const size_t rec0 = (static_cast<size_t>(sg) + pieces[i]) * kParts;
+                const uint32_t dst = smem_u32(stage + i * piece_bytes);
+                bulk_load(dst, rec_acc + rec0 * G * D, acc_bytes, bar);
+                bulk_load(dst + acc_bytes, rec_ml + rec0 * G, ml_bytes, bar);
+            }
+        }
+        // the verdict on the wait must be the same in every thread (they
+        // meet at named barriers below), so the threads vote on it
+        if (!mbar_wait_bounded(bar, phase)) s_stat[192] = 1.f;
+        named_barrier(1, kThreads);
+        if (s_stat[192] != 0.f) {
+            // give copies still in flight one more bounded wait, then stop
+            if (tid == 0) {
+                record_error(err, kErrWaitTimeout);
+                mbar_wait_bounded(bar, phase);
+            }
+            return false;
+        }
+        phase ^= 1u;
+        // running max / sum per row over this chunk's parts
+        if (tid < R) {
+            const int hh = tid / G, r = tid % G;
+            float m_old = s_max[tid], m_new = m_old;
+            for (uint32_t i = 0; i < np; ++i) {
+                const float2* ml = reinterpret_cast<const float2*>(stage + i * piece_bytes + acc_bytes);
+                for (int jj = 0; jj < J; ++jj) m_new = fmaxf(m_new, ml[(hh * J + jj) * G + r].x);
+            }
+            float l = m_old == -INFINITY ? 0.f : s_sum[tid] * exp2f(m_old - m_new);
+            for (uint32_t i = 0; i < np; ++i) {
+                const float2* ml = reinterpret_cast<const float2*>(stage + i * piece_bytes + acc_bytes);
+                for (int jj = 0; jj < J; ++jj) {
+                    const float2 v = ml[(hh * J + jj) * G + r];
+                    if (v.x != -INFINITY) l += v.y * exp2f(v.x - m_new);
+                }
+            }
+            s_scale[tid] = (m_old == -INFINITY) ? 0.f : exp2f(m_old - m_new);
+            s_max[tid] = m_new;
+            s_sum[tid] = l;
+        }
+        named_barrier(1, kThreads);
+#pragma unroll
+        for (int k = 0; k < OPT; ++k) {
+            const int o = tid + kThreads * k;
+            if (o >= nout) continue;
+            const int rr = o / D4, hh = rr / G, r = rr % G, c4 = o % D4;
+            const float mx = s_max[rr], sc = s_scale[rr];
+            float4 a = acc[k];
+            a.x *= sc;
+            a.y *= sc;
+            a.z *= sc;
+            a.w *= sc;
+            for (uint32_t i = 0; i < np; ++i) {
+                const float* pa = reinterpret_cast<const float*>(stage + i * piece_bytes);
+                const float2* ml = reinterpret_cast<const float2*>(stage + i * piece_bytes + acc_bytes);
+#pragma unroll
+                for (int jj = 0; jj < J; ++jj) {
+                    const float mk = ml[(hh * J + jj) * G + r].x;
+                    if (mk == -INFINITY) continue;
+                    const float w = exp2f(mk - mx);
+                    const float4 v = reinterpret_cast<const float4*>(pa + ((hh * J + jj) * G + r) * D)[c4];
+                    a.x += w * v.x;
+                    a.y += w * v.y;
+                    a.z += w * v.z;
+                    a.w += w * v.w;
+                }
+            }
+            acc[k] = a;
+        }
+        named_barrier(1, kThreads);  // the next chunk overwrites the shared records
+    }
+    const uint32_t seq = static_cast<uint32_t>(sg) / head_groups;
+    const uint32_t kv0 = (static_cast<uint32_t>(sg) % head_groups) * HH;
+#pragma unroll
+    for (int k = 0; k < OPT; ++k) {
+        const int o = tid + kThreads * k;
+        if (o < nout) {
+            const int rr = o / D4, hh = rr / G, r = rr % G;
+            const float inv = 1.f / s_sum[rr];
+            __nv_bfloat16* ob =
+                out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kv0 + hh) * G + r) * D + (o % D4) * 4;
+            reinterpret_cast<uint32_t*>(ob)[0] = pack_bf16x2(acc[k].x * inv, acc[k].y * inv);
+            reinterpret_cast<uint32_t*>(ob)[1] = pack_bf16x2(acc[k].z * inv, acc[k].w * inv);
+        }
+    }
+    named_barrier(1, kThreads);  // s_stat is reused by the next merge
+    return true;
 }
 
 template <int D, int HH, int STAGES>
@@ -481,10 +662,8 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     }
     __syncthreads();
     const uint32_t total = static_cast<uint32_t>(prefix[nseg]);
-    if (blockIdx.x == 0)
-        for (int i = tid; i <= nseg; i += kFastThreads) p.seg_prefix[i] = prefix[i];
-    // The combine may be scheduled from here on; it waits (griddepcontrol.wait)
-    // for this whole grid before it reads anything.
+    // The next decode on the stream may be scheduled from here on; it waits
+    // (griddepcontrol.wait) for this whole grid before it touches memory.
     grid_launch_dependents();
     const uint32_t x0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * total / gridDim.x);
     const uint32_t x1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * total / gridDim.x);
@@ -493,12 +672,16 @@ __global__ void __launch_bounds__(kFastThreads, 1)
 
     const uint32_t full0 = smem_u32(bars);
     const uint32_t empty0 = smem_u32(bars + STAGES);
+    __shared__ int s_dead;  // a consumer warp's pipeline wait gave up
+    __shared__ uint32_t s_merge_bits[kStreamMaxSegments / 32];  // segments this CTA merges
+    for (int i = tid; i < kStreamMaxSegments / 32; i += kFastThreads) s_merge_bits[i] = 0u;
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
             mbar_init(empty0 + 8 * s, kFastComputeWarps);
         }
         mbar_fence_init();
+        s_dead = 0;
     }
     __syncthreads();
 
@@ -563,8 +746,6 @@ __global__ void __launch_bounds__(kFastThreads, 1)
                             }
                             const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
                             tma_load_4d(dst + j * S::kBlock, &tmap, full0 + 8 * slot, 0, r, hg * HH, 0, policy);
-                            tma_load_4d(dst + j * S::kBlock + S::kBox, &tmap, full0 + 8 * slot, 0, r + 16,
-                                        hg * HH, 0, policy);
                         }
                     }
                 }
@@ -580,6 +761,8 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     const int g = lane >> 2;
     const int c = lane & 3;
     const int G = static_cast<int>(p.group);
+    const uint32_t grid = gridDim.x;
+    __shared__ float s_stat[196];  // merge: running max, sum, rescale per row; a vote
 
     int sg = sg0;
     uint32_t seg_begin = prefix[sg], seg_end = prefix[sg + 1];
@@ -589,10 +772,14 @@ __global__ void __launch_bounds__(kFastThreads, 1)
 
     uint32_t qa[KS][4];
     WarpState<D> st;
+    bool alive = true;
 
     // Writes this warp's partial (accumulator rows < G, max, sum) for the
-    // current segment piece as record (sg + blockIdx.x, hh, j).
-    auto flush = [&]() {
+    // current segment piece as record (sg + blockIdx.x, hh, j) and counts the
+    // CTA's piece; the CTA whose piece completes the count marks the segment
+    // for merging after its stream. Reached by all consumer warps at the same
+    // stage (segment ends are CTA-uniform).
+    auto finish_piece = [&]() {
         float a0 = st.l0 + __shfl_xor_sync(0xffffffffu, st.l0, 1);
         a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
         float a1 = st.l1 + __shfl_xor_sync(0xffffffffu, st.l1, 1);
@@ -609,13 +796,33 @@ __global__ void __launch_bounds__(kFastThreads, 1)
             if (g < G) p.rec_ml[rec * G + g] = make_float2(st.m0, a0);
             if (g + 8 < G) p.rec_ml[rec * G + g + 8] = make_float2(st.m1, a1);
         }
+        // the records reach L2, for the generic and the async (bulk copy)
+        // proxies, before the arrival is counted
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        __threadfence();
+        named_barrier(1, kFastComputeWarps * 32);
+        if (tid == 0) {
+            uint32_t cf, cl;
+            pieces_of(seg_begin, seg_end, total, grid, cf, cl);
+            uint32_t expected = cl - cf + 1;
+            if (total < grid) {
+                expected = 0;
+                for (uint32_t cc = cf; cc <= cl; ++cc) expected += cta_is_empty(cc, total, grid) ? 0u : 1u;
+            }
+            // the merge itself waits until the CTA's stream is done, so the
+            // pipeline is never held up by it
+            if (expected <= 1 || arrive_last(p.seg_count + sg, p.epoch, expected)) {
+                __threadfence();  // the other pieces' records are read after this
+                s_merge_bits[sg >> 5] |= 1u << (sg & 31);
+            }
+        }
     };
 
     load_query_fragments<D>(qa, p.q, seq, p.hq, hg * HH + hh, G, lane);
     st.reset();
     for (uint32_t x = x0; x < x1; ++x) {
         if (x >= seg_end) {
-            flush();
+            finish_piece();
             do {
                 ++sg;
                 seg_begin = prefix[sg];
@@ -630,198 +837,48 @@ __global__ void __launch_bounds__(kFastThreads, 1)
         }
         const uint32_t it = x - x0;
         const uint32_t slot = it % STAGES;
-        if (!mbar_wait_bounded(full0 + 8 * slot, (it / STAGES) & 1u)) {
-            // no barrier follows, so the warp can stop here; the host sees
-            // the error bit and the combine output is not to be trusted
+        if (alive && !mbar_wait_bounded(full0 + 8 * slot, (it / STAGES) & 1u)) {
+            // the warp stops computing but keeps meeting the CTA's barriers;
+            // the host sees the error bit, and no segment this CTA completes
+            // is merged
             record_error(p.err, kErrWaitTimeout);
-            return;
+            alive = false;
+            s_dead = 1;
         }
         const uint32_t blk = (x - seg_begin) * J + j;
-        if (blk < units) {
+        if (alive && blk < units) {
             const int valid = min(16, ctx - static_cast<int>(blk) * 16);
             const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
-            attend_block<D, HH>(st, qa, kb, kb + S::kBox, hh, valid, p.scale_log2, lane);
+            attend_block<D, HH>(st, qa, kb, hh, valid, p.scale_log2, lane);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty0 + 8 * slot);
     }
-    flush();
-}
-
-constexpr int kCombineThreads = 256;
-constexpr int kCombineWarps = kCombineThreads / 32;
-constexpr int kFewParts = 16;  // partials merged by the one-round-trip path
-
-// Merges the stream-K records of each (segment, kv head) into the output:
-// grid.x = nseg * HH, THREADS threads. Launched as a programmatic dependent of
-// paged_decode_stream; it waits for that grid (griddepcontrol.wait) before
-// reading anything. THREADS is the CTA size (256: measured faster on cfg2
-// than 64 or 128, which fit more of the grid into one wave). The warps split the segment's partial records
-// (warp w takes partials w, w + warps, ...) when there are more than
-// kFewParts of them; each lane keeps its share of the
-// G x D outputs in registers and issues all of a partial's loads at once;
-// the warps' sums meet in shared memory. Dynamic shared memory:
-// (THREADS / 32) * G * D floats.
-template <int D, int HH, int J, int THREADS = kCombineThreads>
-__global__ void __launch_bounds__(THREADS, 512 / THREADS) combine_records(const float* __restrict__ rec_acc,
-                                                                   const float2* __restrict__ rec_ml,
-                                                                   const int32_t* __restrict__ seg_prefix,
-                                                                   __nv_bfloat16* __restrict__ out, uint32_t nseg,
-                                                                   uint32_t head_groups, uint32_t hq, uint32_t group,
-                                                                   uint32_t grid) {
-    constexpr int D4 = D / 4;
-    constexpr int kMaxOut = 16 * D4 / 32;  // float4 outputs per lane for G = 16
-    extern __shared__ float4 partial_sums[];  // [warps][G * D4]
-    __shared__ float s_max[(THREADS / 32)][16];
-    __shared__ float s_sum[(THREADS / 32)][16];
-    grid_dependency_wait();
-    // the next decode may start its prologue while this grid runs
-    grid_launch_dependents();
-    const uint32_t sg = blockIdx.x / HH;
-    const int hh = blockIdx.x % HH;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t ps = static_cast<uint32_t>(seg_prefix[sg]);
-    const uint32_t pe = static_cast<uint32_t>(seg_prefix[sg + 1]);
-    const uint32_t total = static_cast<uint32_t>(seg_prefix[nseg]);
-    if (pe <= ps) return;
-    // CTAs whose stage ranges intersect [ps, pe)
-    const uint32_t cf = static_cast<uint32_t>((static_cast<uint64_t>(ps + 1) * grid - 1) / total);
-    const uint32_t cl = static_cast<uint32_t>((static_cast<uint64_t>(pe) * grid - 1) / total);
-    const int G = static_cast<int>(group);
-    const int nout = G * D4;
-    const int nparts = static_cast<int>(cl - cf + 1) * J;
-    const bool may_be_empty = total < grid;
-    // record of part k: CTA cf + k / J, warp column k % J
-    auto rec_of = [&](int k) { return ((static_cast<size_t>(sg) + cf + k / J) * HH + hh) * J + (k % J); };
-    auto usable = [&](int k) { return !may_be_empty || !cta_is_empty(cf + k / J, total, grid); };
-    const uint32_t seq = sg / head_groups;
-    const uint32_t kvh = (sg % head_groups) * HH + hh;
-    __nv_bfloat16* ob = out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kvh) * G) * D;
-
-    if (nparts <= kFewParts) {
-        // Few partials (the common case): every (row, partial) max/sum in
-        // one round trip, normalised weights in shared memory, then each
-        // thread issues all partial loads of one output before summing.
-        __shared__ float2 sml[16][kFewParts];
-        __shared__ float sw[16][kFewParts];
-        __shared__ float sinv[16];
-        for (int i = threadIdx.x; i < G * nparts; i += THREADS) {
-            const int r = i / nparts, k = i % nparts;
-            sml[r][k] = usable(k) ? rec_ml[rec_of(k) * G + r] : make_float2(-INFINITY, 0.f);
-        }
-        __syncthreads();
-        if (threadIdx.x < G) {
-            const int r = threadIdx.x;
-            float M = -INFINITY;
-            for (int k = 0; k < nparts; ++k) M = fmaxf(M, sml[r][k].x);
-            float L = 0.f;
-            for (int k = 0; k < kFewParts; ++k) {
-                const float2 ml = k < nparts ? sml[r][k] : make_float2(-INFINITY, 0.f);
-                const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
-                sw[r][k] = w;
-                L += w * ml.y;
-            }
-            sinv[r] = 1.f / L;
-        }
-        __syncthreads();
-        for (int o = threadIdx.x; o < nout; o += THREADS) {
-            const int r = o / D4;
-            float4 v[kFewParts];
-#pragma unroll
-            for (int k = 0; k < kFewParts; ++k)
-                if (k < nparts && sw[r][k] != 0.f)
-                    v[k] = reinterpret_cast<const float4*>(rec_acc + rec_of(k) * G * D)[o];
-            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int k = 0; k < kFewParts; ++k) {
-                const float w = k < nparts ? sw[r][k] : 0.f;
-                if (w != 0.f) {
-                    a.x += w * v[k].x;
-                    a.y += w * v[k].y;
-                    a.z += w * v[k].z;
-                    a.w += w * v[k].w;
-                }
-            }
-            const float inv = sinv[r];
-            *reinterpret_cast<uint32_t*>(ob + o * 4) = pack_bf16x2(a.x * inv, a.y * inv);
-            *reinterpret_cast<uint32_t*>(ob + o * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
-        }
-        return;
+    finish_piece();
+    named_barrier(1, kFastComputeWarps * 32);
+    if (s_dead != 0) return;  // records of this CTA are not to be trusted: merge nothing
+    // Merge the segments whose last piece this CTA completed (sg0 .. sg),
+    // through the pipeline's shared memory (the stream is done with it).
+    const int nout = HH * G * (D / 4);
+    __shared__ __align__(8) uint64_t s_merge_bar;
+    const uint32_t mbar = smem_u32(&s_merge_bar);
+    if (tid == 0) {
+        mbar_init(mbar, 1);
+        mbar_fence_init();
     }
-
-    // Many partials: the warps split them (warp w takes w, w+8, ...).
-    // per-row maximum over this warp's partials (lane r holds row r)
-    float m = -INFINITY;
-    if (lane < G)
-        for (int k = warp; k < nparts; k += (THREADS / 32))
-            if (usable(k)) m = fmaxf(m, rec_ml[rec_of(k) * G + lane].x);
-    if (lane < 16) s_max[warp][lane] = m;
-    __syncthreads();
-    float M = -INFINITY;
-    if (lane < G)
-        for (int w = 0; w < (THREADS / 32); ++w) M = fmaxf(M, s_max[w][lane]);
-
-    // outputs in chunks of kChunk float4 per lane (all of a partial's loads
-    // for one chunk are issued together)
-    constexpr int kChunk = 8;
-    float lsum = 0.f;
-    for (int c0 = 0; c0 < kMaxOut; c0 += kChunk) {
-        if (32 * c0 >= nout) break;
-        float4 acc[kChunk];
-#pragma unroll
-        for (int i = 0; i < kChunk; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int k = warp; k < nparts; k += (THREADS / 32)) {
-            if (!usable(k)) continue;
-            const size_t rec = rec_of(k);
-            // weight of row `lane` in this partial, shared with the warp by shfl
-            float wr = 0.f;
-            if (lane < G) {
-                const float2 ml = rec_ml[rec * G + lane];
-                wr = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - M);
-                if (c0 == 0) lsum += wr * ml.y;
-            }
-            const float4* src = reinterpret_cast<const float4*>(rec_acc + rec * G * D);
-            float4 v[kChunk];
-#pragma unroll
-            for (int i = 0; i < kChunk; ++i) {
-                const int o = lane + 32 * (c0 + i);
-                if (o < nout) v[i] = src[o];
-            }
-#pragma unroll
-            for (int i = 0; i < kChunk; ++i) {
-                const int o = lane + 32 * (c0 + i);
-                const float w = __shfl_sync(0xffffffffu, wr, (o < nout ? o : 0) / D4);
-                if (o < nout) {
-                    acc[i].x += w * v[i].x;
-                    acc[i].y += w * v[i].y;
-                    acc[i].z += w * v[i].z;
-                    acc[i].w += w * v[i].w;
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < kChunk; ++i) {
-            const int o = lane + 32 * (c0 + i);
-            if (o < nout) partial_sums[warp * nout + o] = acc[i];
-        }
-    }
-    if (lane < 16) s_sum[warp][lane] = lsum;
-    __syncthreads();
-    for (int o = threadIdx.x; o < nout; o += THREADS) {
-        const int r = o / D4;
-        float L = 0.f;
-        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int w = 0; w < (THREADS / 32); ++w) {
-            L += s_sum[w][r];
-            const float4 v = partial_sums[w * nout + o];
-            a.x += v.x;
-            a.y += v.y;
-            a.z += v.z;
-            a.w += v.w;
-        }
-        const float inv = 1.f / L;
-        *reinterpret_cast<uint32_t*>(ob + o * 4) = pack_bf16x2(a.x * inv, a.y * inv);
-        *reinterpret_cast<uint32_t*>(ob + o * 4 + 2) = pack_bf16x2(a.z * inv, a.w * inv);
+    named_barrier(1, kFastComputeWarps * 32);
+    uint32_t phase = 0;
+    for (int ms = sg0; ms <= sg; ++ms) {
+        if ((s_merge_bits[ms >> 5] & (1u << (ms & 31))) == 0) continue;
+        uint32_t cf, cl;
+        pieces_of(static_cast<uint32_t>(prefix[ms]), static_cast<uint32_t>(prefix[ms + 1]), total, grid, cf, cl);
+#define QVP_MERGE(OPT)                                                                                              \
+    merge_segment<D, HH, J, OPT>(p.rec_acc, p.rec_ml, p.out, p.group, p.head_groups, p.hq, ms, cf, cl, total, grid, \
+                                 smem, STAGES * S::kStage, mbar, phase, s_stat, tid, p.err)
+        const bool merged = nout <= 256 ? QVP_MERGE(1) : nout <= 512 ? QVP_MERGE(2) : nout <= 1024 ? QVP_MERGE(4)
+                                                                                          : QVP_MERGE(8);
+#undef QVP_MERGE
+        if (!merged) break;
     }
 }
 
@@ -1014,9 +1071,10 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 }  // namespace
 
-// The pool viewed as a 4-D tensor of bf16 so one TMA box is the K (or V)
-// slice of one block for HH consecutive kv heads, laid out in shared memory
-// as [head_dim/64][HH][16 tokens][64]:
+// The pool viewed as a 4-D tensor of bf16 so one TMA box is the K and V
+// slices of one block for HH consecutive kv heads, laid out in shared memory
+// as [head_dim/64][HH][16 K rows, then 16 V rows][64] (K and V of a block
+// are adjacent token rows, so one box carries both: one TMA copy per block):
 //   dim0: 64 elements of head_dim        (contiguous)
 //   dim1: token rows of the whole pool   (stride kv_heads*head_dim*2 bytes)
 //   dim2: kv head                        (stride head_dim*2 bytes)
@@ -1028,7 +1086,7 @@ int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape
                     CUtensorMap* map) {
     struct Key {
         const void* pool;
-        uint32_t num_blocks, layers, heads, dim, hh;
+        uint32_t num_blocks, layers, heads, dim, hh, rows;
     };
     static thread_local Key last{};
     static thread_local CUtensorMap cached;
@@ -1041,6 +1099,7 @@ int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape
     key.heads = shape.num_kv_heads;
     key.dim = shape.head_dim;
     key.hh = hh;
+    key.rows = 32;
     if (std::memcmp(&key, &last, sizeof(Key)) == 0) {
         *map = cached;
         return QVP_OK;
@@ -1051,7 +1110,7 @@ int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape
     const uint32_t H = shape.num_kv_heads;
     cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(num_blocks) * shape.num_layers * 2 * 16, H, D / 64};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(H) * D * 2, static_cast<cuuint64_t>(D) * 2, 128};
-    cuuint32_t box[4] = {64, 16, hh, D / 64};
+    cuuint32_t box[4] = {64, 32, hh, D / 64};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(pool), dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -1089,34 +1148,6 @@ int launch_fast(const qvp_decode_args& a, const DecodePlan& plan, const FastPara
     }
 }
 
-// The combine is a programmatic dependent: it may be scheduled while the
-// decode grid still runs and waits (griddepcontrol.wait) for its results.
-template <int D, int HH, int J, int THREADS>
-int launch_combine(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
-    constexpr int kWarps = THREADS / 32;
-    static std::atomic<std::uint64_t> attr_done{0};
-    auto kern = combine_records<D, HH, J, THREADS>;
-    const int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern),
-                                       kWarps * 16 * D * static_cast<int>(sizeof(float)), "cudaFuncSetAttribute(combine)");
-    if (rc != QVP_OK) return rc;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(sp.nseg * HH);
-    cfg.blockDim = dim3(THREADS);
-    cfg.dynamicSmemBytes = static_cast<size_t>(kWarps) * sp.group * D * sizeof(float);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return check_cuda(cudaLaunchKernelEx(&cfg, kern, static_cast<const float*>(sp.rec_acc),
-                                         static_cast<const float2*>(sp.rec_ml),
-                                         static_cast<const int32_t*>(sp.seg_prefix),
-                                         static_cast<__nv_bfloat16*>(a.out), sp.nseg, sp.head_groups, sp.hq,
-                                         sp.group, plan.grid_ctas),
-                      "launch combine_records");
-}
-
 template <int D, int HH, int STAGES>
 int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
     using S = FastShape<D, HH, STAGES>;
@@ -1131,10 +1162,10 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
     CUtensorMap map;
     rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
     if (rc != QVP_OK) return rc;
-    const uint32_t smem = S::kSmem + (sp.nseg + 1) * 4;
+    const uint32_t smem = kMaxSmem;
     {
         // programmatic dependent of whatever precedes it on the stream (the
-        // previous step's combine): the prologue overlaps that kernel's tail
+        // previous step's decode): the prologue overlaps that kernel's tail
         cudaLaunchConfig_t dcfg = {};
         dcfg.gridDim = dim3(plan.grid_ctas);
         dcfg.blockDim = dim3(kFastThreads);
@@ -1145,11 +1176,8 @@ int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const Stre
         dattr[0].val.programmaticStreamSerializationAllowed = 1;
         dcfg.attrs = dattr;
         dcfg.numAttrs = 1;
-        rc = check_cuda(cudaLaunchKernelEx(&dcfg, kern, map, sp), "launch stream decode");
-        if (rc != QVP_OK) return rc;
+        return check_cuda(cudaLaunchKernelEx(&dcfg, kern, map, sp), "launch stream decode");
     }
-
-    return launch_combine<D, HH, J, kCombineThreads>(a, plan, sp, st);
 }
 
 int launch_stream(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
@@ -1159,6 +1187,15 @@ int launch_stream(const qvp_decode_args& a, const DecodePlan& plan, const Stream
         case 2: return D == 128 ? launch_stream_t<128, 2, 3>(a, plan, sp, st) : launch_stream_t<64, 2, 6>(a, plan, sp, st);
         default: return D == 128 ? launch_stream_t<128, 1, 3>(a, plan, sp, st) : launch_stream_t<64, 1, 6>(a, plan, sp, st);
     }
+}
+
+// Epoch of a stream-K launch: distinct for every launch of this process and,
+// through the clock seed, unlikely to match a word another process left in
+// recycled device memory.
+uint32_t next_epoch() {
+    static std::atomic<uint32_t> epoch{static_cast<uint32_t>(
+        std::chrono::steady_clock::now().time_since_epoch().count() * 2654435761ull)};
+    return epoch.fetch_add(1, std::memory_order_relaxed) + 1u;
 }
 
 }  // namespace
@@ -1217,7 +1254,7 @@ int plan_decode(const qvp_decode_args& a, DecodePlan& plan) {
             plan.max_splits = 1;
             plan.workspace_bytes = round_up(records * plan.group * sh.head_dim * sizeof(float), 256) +
                                    round_up(records * plan.group * sizeof(float2), 256) +
-                                   (static_cast<size_t>(plan.nseg) + 1) * sizeof(int32_t);
+                                   static_cast<size_t>(plan.nseg) * sizeof(unsigned long long);
             return QVP_OK;
         }
     }
@@ -1304,7 +1341,9 @@ int qvp::run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream
         sp.q = static_cast<const __nv_bfloat16*>(a.query);
         sp.rec_acc = reinterpret_cast<float*>(ws);
         sp.rec_ml = reinterpret_cast<float2*>(ws + acc_bytes);
-        sp.seg_prefix = reinterpret_cast<int32_t*>(ws + acc_bytes + ml_bytes);
+        sp.seg_count = reinterpret_cast<unsigned long long*>(ws + acc_bytes + ml_bytes);
+        sp.out = static_cast<__nv_bfloat16*>(a.out);
+        sp.epoch = next_epoch();
         sp.err = a.error_word;
         sp.pitch = a.max_blocks_per_seq;
         sp.num_blocks = a.num_blocks;

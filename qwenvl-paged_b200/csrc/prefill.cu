@@ -54,19 +54,19 @@ struct PrefillParams {
 
 template <int D, int NB, int STAGES>
 struct PrefillShape {
-    static constexpr uint32_t kBox = 16 * D * 2;      // one stream of one block, one head
-    static constexpr uint32_t kBlock = 2 * kBox;      // K and V
+    static constexpr uint32_t kBlock = 2 * 16 * D * 2;  // K and V of one block, one head (one TMA box)
     static constexpr uint32_t kStage = NB * kBlock;
     static constexpr uint32_t kSmem = STAGES * kStage + 1024 + 2 * STAGES * 8 + 16;
 };
 
 // attend_block with a separate causal limit for each of the lane's two rows:
 // `va` / `vb` keys of this block are visible to rows g and g+8, and `vctx`
-// slots hold real data (V past it is zeroed).
+// slots hold real data (V past it is zeroed). `blk` is the block's box
+// [head_dim/64][K 16 | V 16 tokens][64]: K rows of dh are row group 2*dh, V
+// rows row group 2*dh+1.
 template <int D>
-__device__ __forceinline__ void attend_block_rows(WarpState<D>& st, const uint32_t (&qa)[D / 16][4], uint32_t kb,
-                                                  uint32_t vb, int va, int vb_rows, int vctx, float scale_log2,
-                                                  int lane) {
+__device__ __forceinline__ void attend_block_rows(WarpState<D>& st, const uint32_t (&qa)[D / 16][4], uint32_t blk,
+                                                  int va, int vb_rows, int vctx, float scale_log2, int lane) {
     const int c = lane & 3;
     const int mi = lane >> 3;
     const int li = lane & 7;
@@ -79,7 +79,7 @@ __device__ __forceinline__ void attend_block_rows(WarpState<D>& st, const uint32
         const int chunk = ((ks & 3) << 1) + (mi & 1);
         const int t = ((mi >> 1) << 3) + li;
         uint32_t r0, r1, r2, r3;
-        ldmatrix_x4(box_addr(kb, dh, t, chunk), r0, r1, r2, r3);
+        ldmatrix_x4(box_addr(blk, 2 * dh, t, chunk), r0, r1, r2, r3);
         mma_bf16_16816(s[0], qa[ks], r0, r1);
         mma_bf16_16816(s[1], qa[ks], r2, r3);
     }
@@ -131,7 +131,7 @@ __device__ __forceinline__ void attend_block_rows(WarpState<D>& st, const uint32
         const int chunk = ((np & 3) << 1) + (mi >> 1);
         const int t = ((mi & 1) << 3) + li;
         uint32_t v0, v1, v2, v3;
-        ldmatrix_x4_trans(box_addr(vb, dh, t, chunk), v0, v1, v2, v3);
+        ldmatrix_x4_trans(box_addr(blk, 2 * dh + 1, t, chunk), v0, v1, v2, v3);
         if (vctx < 16) {
             v0 = mask_pair(v0, c * 2, vctx);
             v2 = mask_pair(v2, c * 2, vctx);
@@ -210,7 +210,6 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
                     }
                     const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
                     tma_load_4d(dst + j * S::kBlock, &tmap, full0 + 8 * slot, 0, r, kvh, 0, policy);
-                    tma_load_4d(dst + j * S::kBlock + S::kBox, &tmap, full0 + 8 * slot, 0, r + 16, kvh, 0, policy);
                 }
             }
         }
@@ -267,7 +266,7 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
                 const int vbr = max(0, min(16, pos_b - k0 + 1));
                 const int vctx = min(16, ctx - k0);
                 const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
-                attend_block_rows<D>(st, qa, kb, kb + S::kBox, va, vbr, vctx, p.scale_log2, lane);
+                attend_block_rows<D>(st, qa, kb, va, vbr, vctx, p.scale_log2, lane);
             }
         }
         __syncwarp();

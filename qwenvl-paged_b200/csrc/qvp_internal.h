@@ -57,9 +57,9 @@ struct CUtensorMap_st;
 namespace qvp {
 
 // Encodes (and caches, per thread) the TMA view of a bf16 pool in which one
-// box is the K or V slice of one block for `hh` consecutive kv heads, laid
-// out in shared memory as [head_dim/64][hh][16 tokens][64] with 128-byte
-// swizzle. Needs unpadded blocks (stride == byte size).
+// box is the K and V slices of one block for `hh` consecutive kv heads, laid
+// out in shared memory as [head_dim/64][hh][16 K rows, 16 V rows][64] with
+// 128-byte swizzle. Needs unpadded blocks (stride == byte size).
 int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape& shape, uint32_t hh,
                     CUtensorMap_st* map);
 

@@ -94,8 +94,18 @@ public:
     // ---- device-pool additions (no counterpart in the reference) ----------
     // Enqueues all deferred copies and swap moves on the engine stream.
     void flush();
-    // flush() and wait for the engine stream.
+    // flush() and wait (bounded) for the engine stream and the swap moves.
     bool synchronize();
+    // Make the engine stream wait for enqueued swap moves that device work
+    // about to be enqueued on it depends on: order_reads for work that reads
+    // the `n` listed frames (null: any frame; entries < 0 ignored) and waits
+    // only for loads into them; order_writes for work that writes the pool,
+    // which waits for every enqueued move. Both are no-ops without a swap
+    // backend that defers moves.
+    void order_reads(const std::int32_t* frames, std::size_t n);
+    void order_writes();
+    // True while a swap-in enqueued by flush() may not have landed yet.
+    [[nodiscard]] bool loads_in_flight() const;
     // Synchronous host <-> block byte moves for set-up and tests.
     bool write_bytes(PhysicalBlockId id, std::size_t offset, const void* host, std::size_t bytes);
     bool read_bytes(PhysicalBlockId id, std::size_t offset, void* host, std::size_t bytes);

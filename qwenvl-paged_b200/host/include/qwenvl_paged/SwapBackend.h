@@ -20,6 +20,9 @@
 #include <unordered_map>
 #include <vector>
 
+struct CUstream_st;
+struct CUevent_st;
+
 namespace qwenvl_paged {
 
 class MemoryAllocator;
@@ -31,11 +34,24 @@ public:
     [[nodiscard]] virtual bool load(SwapSlotId slot, PhysicalBlock& block) = 0;
     virtual void discard(SwapSlotId slot) = 0;
     [[nodiscard]] virtual std::size_t resident_slots() const noexcept = 0;
-    // Enqueues any store/load data movement the backend has deferred, on the
-    // allocator's stream. The allocator calls it before it enqueues other
-    // device work, so deferred moves keep program order. Backends that move
-    // bytes eagerly need not override it.
+    // ---- device-pool additions (no counterpart in the reference) ----------
+    // Enqueues any store/load data movement the backend has deferred, after
+    // all device work already on the allocator's stream. The allocator calls
+    // it before it enqueues other device work. Backends that move bytes
+    // eagerly need not override these.
     virtual void flush() {}
+    // Makes `engine` (the allocator's stream) wait for enqueued moves that
+    // device work about to be enqueued there depends on: with `writes`, every
+    // enqueued move (a write may land on a frame a store still reads, or on
+    // a loaded frame); otherwise only loads into the `n` frames listed
+    // (`frames` null: into any frame). Entries < 0 are ignored.
+    virtual void order_engine(CUstream_st* /*engine*/, const std::int32_t* /*frames*/, std::size_t /*n*/,
+                              bool /*writes*/) {}
+    // True while a load enqueued by flush() may not have landed yet.
+    [[nodiscard]] virtual bool loads_in_flight() const { return false; }
+    // Waits (bounded) until every enqueued move has landed; false on a
+    // timeout or a device error.
+    virtual bool wait_idle() { return true; }
 };
 
 // Host-heap swap space with the reference's behaviour: each store copies the
@@ -64,11 +80,18 @@ private:
 
 // Pinned-host swap space for a device pool. `store` and `load` only record
 // the move (slot bookkeeping is immediate, so the allocator's frame and slot
-// decisions are exactly the reference's); `flush` turns all recorded stores
-// into one gather kernel into device staging plus one cudaMemcpyAsync per
-// contiguous run of slab slots, and all recorded loads into the reverse.
-// The slab holds `max_slots` blocks of the allocator's block stride and is
-// allocated once (cudaHostAlloc) at construction.
+// decisions are exactly the reference's); `flush` enqueues them on a copy
+// stream of the backend's own, after the engine work already enqueued:
+// recorded stores as gather kernels into device staging plus one
+// cudaMemcpyAsync per contiguous run of slab slots, recorded loads as the
+// reverse. The engine stream goes on meanwhile: decode of sequences that are
+// not being loaded overlaps the PCIe traffic. Work that writes the pool waits
+// for every enqueued move first, and work that reads a frame being loaded
+// waits for the loads (order_engine, called by the allocator and the decode
+// batches). Everything the moves need (the slab, device staging, the block-id
+// lists, the copy stream and its events) is allocated at construction, so a
+// move once recorded is never dropped; if any of it cannot be had, ready() is
+// false and every store is refused, leaving the bookkeeping untouched.
 class DeviceSwapBackend final : public SwapBackend {
 public:
     DeviceSwapBackend(MemoryAllocator& allocator, std::size_t max_slots);
@@ -81,18 +104,24 @@ public:
     void discard(SwapSlotId slot) override;
     [[nodiscard]] std::size_t resident_slots() const noexcept override;
     void flush() override;
+    void order_engine(CUstream_st* engine, const std::int32_t* frames, std::size_t n, bool writes) override;
+    [[nodiscard]] bool loads_in_flight() const override;
+    bool wait_idle() override;
 
     [[nodiscard]] std::size_t capacity_slots() const noexcept;
-    // False when the pinned slab could not be allocated (every store fails).
+    // False when a buffer of the backend could not be allocated (every store
+    // is refused).
     [[nodiscard]] bool ready() const noexcept;
     // Host address of a resident slot's bytes (for tests), null if unknown.
-    // Valid once the stream has passed the flush that filled it.
+    // Valid once wait_idle() has returned after the flush that filled it.
     [[nodiscard]] const std::byte* slot_bytes(SwapSlotId slot) const noexcept;
     // Bytes moved between pool and slab so far, in each direction.
     [[nodiscard]] std::uint64_t bytes_out() const noexcept { return bytes_out_; }
     [[nodiscard]] std::uint64_t bytes_in() const noexcept { return bytes_in_; }
-    // Text of the first failure of a flush (empty when every move was
-    // enqueued). A failed store flush loses the bytes of the blocks it held.
+    // The copy stream the moves run on.
+    [[nodiscard]] CUstream_st* copy_stream() const noexcept { return copy_; }
+    // Text of the first failure (a launch error or a timed-out wait); empty
+    // when every move was enqueued.
     [[nodiscard]] const std::string& last_error() const noexcept { return error_; }
 
 private:
@@ -100,10 +129,9 @@ private:
         std::int32_t block;
         std::uint32_t slab_index;
     };
-    void flush_stores();
-    void flush_loads();
-    bool ensure_staging(std::size_t blocks);
+    void flush_moves(std::vector<Move>& moves, bool stores, std::int32_t* ids_dev);
     void note(const std::string& what);  // keeps the first error
+    void refresh_loads() const;
 
     MemoryAllocator* allocator_{nullptr};
     std::size_t max_slots_{0};
@@ -111,10 +139,20 @@ private:
     std::byte* slab_{nullptr};            // pinned host, max_slots * slot_bytes
     std::byte* staging_{nullptr};         // device, staging_blocks_ * slot_bytes
     std::size_t staging_blocks_{0};
-    std::int32_t* ids_host_{nullptr};     // pinned block-id list for one flush
-    std::int32_t* ids_dev_{nullptr};
-    std::size_t ids_capacity_{0};
-    void* ids_event_{nullptr};            // cudaEvent_t: the last id-list upload
+    // two block-id lists (pinned + device) of 2 * max_slots entries; flushes
+    // alternate between them
+    std::int32_t* ids_host_[2]{nullptr, nullptr};
+    std::int32_t* ids_dev_[2]{nullptr, nullptr};
+    CUevent_st* ids_uploaded_[2]{nullptr, nullptr};  // the list's last upload
+    int ids_next_{0};
+    CUstream_st* copy_{nullptr};
+    CUevent_st* engine_mark_{nullptr};    // the engine stream at the last flush
+    CUevent_st* moves_done_{nullptr};     // copy stream after the last flush
+    std::uint64_t flush_seq_{0};          // flushes with moves so far
+    std::uint64_t engine_waited_{0};      // flushes the engine already waits for
+    std::uint64_t last_load_flush_{0};    // newest flush that carried loads
+    mutable std::uint64_t done_seq_{0};   // flushes known to have landed
+    std::vector<std::uint64_t> frame_load_flush_;  // per frame: flush that loaded it
     SwapSlotId next_slot_{1};
     std::unordered_map<SwapSlotId, std::uint32_t> slots_;  // resident slot -> slab index
     std::set<std::uint32_t> free_indices_;

@@ -77,12 +77,14 @@ int read_error_word(const MemoryAllocator& alloc, const std::int32_t* err) {
 }
 
 // Copies `staged` into the pinned buffer (once the previous upload has left
-// it), lands queued copy-on-write copies and swap moves, then uploads.
+// it), lands queued copy-on-write copies and swap moves (the kernel that
+// follows waits for every enqueued swap move), then uploads.
 void upload(MemoryAllocator& alloc, const std::vector<std::int32_t>& staged, std::int32_t* host, std::int32_t* dev,
             void* event) {
-    cudaEventSynchronize(static_cast<cudaEvent_t>(event));
+    host_impl::wait_event(static_cast<cudaEvent_t>(event), "index upload", nullptr);
     std::memcpy(host, staged.data(), staged.size() * sizeof(std::int32_t));
     alloc.flush();
+    alloc.order_writes();
     cudaMemcpyAsync(dev, host, staged.size() * sizeof(std::int32_t), cudaMemcpyHostToDevice, alloc.stream());
     cudaEventRecord(static_cast<cudaEvent_t>(event), alloc.stream());
 }

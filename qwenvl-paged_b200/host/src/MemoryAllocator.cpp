@@ -1,5 +1,6 @@
 #include "qwenvl_paged/MemoryAllocator.h"
 
+#include "host_impl.h"
 #include "qvp.h"
 
 #include <cuda_runtime.h>
@@ -48,13 +49,34 @@ MemoryAllocator::MemoryAllocator(AllocatorConfig config, DevicePoolOptions optio
         void* p = nullptr;
         const std::size_t total = stride_ * config_.max_blocks;
         const cudaError_t e = host_visible_ ? cudaMallocManaged(&p, total, cudaMemAttachGlobal) : cudaMalloc(&p, total);
-        if (e == cudaSuccess) {
+        // The copy-pair lists are sized for the most copies one flush can
+        // carry (pending copies have distinct destinations), so a queued copy
+        // never waits on an allocation that could fail.
+        const std::size_t pair_ints = 2 * static_cast<std::size_t>(config_.max_blocks);
+        cudaEvent_t ev = nullptr;
+        const bool ok = e == cudaSuccess &&
+                        cudaMalloc(reinterpret_cast<void**>(&pairs_dev_), pair_ints * sizeof(std::int32_t)) ==
+                            cudaSuccess &&
+                        cudaMallocHost(reinterpret_cast<void**>(&pairs_host_), pair_ints * sizeof(std::int32_t)) ==
+                            cudaSuccess &&
+                        cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess;
+        if (ok) {
             pool_ = static_cast<std::byte*>(p);
+            pairs_capacity_ = pair_ints;
+            pairs_event_ = ev;
             cudaMemset(pool_, 0, total);
             cudaDeviceSynchronize();
         } else {
+            const cudaError_t why = e != cudaSuccess ? e : cudaGetLastError();
             cudaGetLastError();
-            error_ = std::string("cudaMalloc of the block pool failed: ") + cudaGetErrorString(e);
+            error_ = std::string("device storage of the block pool could not be allocated: ") +
+                     cudaGetErrorString(why);
+            if (p != nullptr && e == cudaSuccess) cudaFree(p);
+            if (pairs_dev_ != nullptr) cudaFree(pairs_dev_);
+            if (pairs_host_ != nullptr) cudaFreeHost(pairs_host_);
+            if (ev != nullptr) cudaEventDestroy(ev);
+            pairs_dev_ = nullptr;
+            pairs_host_ = nullptr;
         }
     }
 
@@ -74,7 +96,7 @@ MemoryAllocator::~MemoryAllocator() { release_storage(); }
 
 void MemoryAllocator::release_storage() noexcept {
     DeviceGuard guard(device_);
-    if (pool_ != nullptr || pairs_dev_ != nullptr) cudaStreamSynchronize(stream_);
+    if (pool_ != nullptr || pairs_dev_ != nullptr) host_impl::wait_stream(stream_, "allocator teardown", nullptr);
     if (pool_ != nullptr) cudaFree(pool_);
     if (pairs_dev_ != nullptr) cudaFree(pairs_dev_);
     if (pairs_host_ != nullptr) cudaFreeHost(pairs_host_);
@@ -159,7 +181,7 @@ void MemoryAllocator::copy_block(PhysicalBlockId source, PhysicalBlockId destina
         // host code may read or write either block next: the copy lands now
         flush_copies();
         DeviceGuard guard(device_);
-        if (cudaStreamSynchronize(stream_) != cudaSuccess) error_ = cudaGetErrorString(cudaGetLastError());
+        host_impl::wait_stream(stream_, "copy-on-write copy", &error_);
     }
 }
 
@@ -167,40 +189,11 @@ void MemoryAllocator::flush_copies() {
     if (pending_pairs_.empty()) return;
     DeviceGuard guard(device_);
     const std::size_t n = pending_pairs_.size();
-    if (n > pairs_capacity_) {
-        if (pairs_event_ != nullptr) cudaEventSynchronize(static_cast<cudaEvent_t>(pairs_event_));
-        if (pairs_dev_ != nullptr) cudaFree(pairs_dev_);
-        if (pairs_host_ != nullptr) cudaFreeHost(pairs_host_);
-        const std::size_t cap = n < 1024 ? 1024 : 2 * n;
-        pairs_dev_ = nullptr;
-        pairs_host_ = nullptr;
-        pairs_capacity_ = 0;
-        if (cudaMalloc(reinterpret_cast<void**>(&pairs_dev_), cap * sizeof(std::int32_t)) != cudaSuccess ||
-            cudaMallocHost(reinterpret_cast<void**>(&pairs_host_), cap * sizeof(std::int32_t)) != cudaSuccess) {
-            cudaGetLastError();
-            error_ = "could not allocate the copy-pair buffers";
-            pending_pairs_.clear();
-            pending_src_.clear();
-            pending_dst_.clear();
-            return;
-        }
-        pairs_capacity_ = cap;
-    }
-    if (pairs_event_ == nullptr) {
-        cudaEvent_t ev = nullptr;
-        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
-            cudaGetLastError();
-            error_ = "could not create the copy-pair event";
-            pending_pairs_.clear();
-            pending_src_.clear();
-            pending_dst_.clear();
-            return;
-        }
-        pairs_event_ = ev;
-    } else {
-        // the pinned list of the previous flush must have reached the device
-        cudaEventSynchronize(static_cast<cudaEvent_t>(pairs_event_));
-    }
+    // the copies write frames a swap move may still read, or read frames a
+    // swap-in is still filling
+    if (swap_backend_ != nullptr) swap_backend_->order_engine(stream_, nullptr, 0, true);
+    // the pinned list of the previous flush must have reached the device
+    if (!host_impl::wait_event(static_cast<cudaEvent_t>(pairs_event_), "copy-pair upload", &error_)) return;
     std::memcpy(pairs_host_, pending_pairs_.data(), n * sizeof(std::int32_t));
     cudaMemcpyAsync(pairs_dev_, pairs_host_, n * sizeof(std::int32_t), cudaMemcpyHostToDevice, stream_);
     cudaEventRecord(static_cast<cudaEvent_t>(pairs_event_), stream_);
@@ -222,12 +215,28 @@ void MemoryAllocator::flush() {
 bool MemoryAllocator::synchronize() {
     flush();
     DeviceGuard guard(device_);
-    const cudaError_t e = cudaStreamSynchronize(stream_);
-    if (e != cudaSuccess) {
-        error_ = cudaGetErrorString(e);
+    if (!host_impl::wait_stream(stream_, "engine stream", &error_)) return false;
+    if (swap_backend_ != nullptr && !swap_backend_->wait_idle()) {
+        if (error_.empty()) error_ = "swap moves did not complete";
         return false;
     }
     return error_.empty();
+}
+
+void MemoryAllocator::order_reads(const std::int32_t* frames, std::size_t n) {
+    if (swap_backend_ == nullptr) return;
+    DeviceGuard guard(device_);
+    swap_backend_->order_engine(stream_, frames, n, false);
+}
+
+void MemoryAllocator::order_writes() {
+    if (swap_backend_ == nullptr) return;
+    DeviceGuard guard(device_);
+    swap_backend_->order_engine(stream_, nullptr, 0, true);
+}
+
+bool MemoryAllocator::loads_in_flight() const {
+    return swap_backend_ != nullptr && swap_backend_->loads_in_flight();
 }
 
 bool MemoryAllocator::write_bytes(PhysicalBlockId id, std::size_t offset, const void* host, std::size_t bytes) {

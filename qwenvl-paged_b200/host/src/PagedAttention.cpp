@@ -55,6 +55,7 @@ bool decode_one(const CacheView& view, const void* query, std::size_t elem_bytes
     if (!alloc.has_storage() || dtype_for(elem_bytes) < 0) return false;
     OnDevice guard(alloc.device());
     alloc.flush();  // queued copy-on-write copies land before the decode reads
+    alloc.order_reads(ids.data(), ids.size());  // and swap-ins into its frames
 
     const BlockShape& sh = view.layout.shape;
     const std::size_t qo_bytes = static_cast<std::size_t>(params.num_query_heads) * sh.head_dim * elem_bytes;
@@ -199,7 +200,10 @@ bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vecto
         return false;
     }
     // the previous step's upload must have left the pinned buffer
-    cudaEventSynchronize(static_cast<cudaEvent_t>(upload_event_));
+    if (!host_impl::wait_event(static_cast<cudaEvent_t>(upload_event_), "table upload", &error_)) {
+        status_ = QVP_ERR_CUDA;
+        return false;
+    }
     for (std::size_t b = 0; b < B; ++b) {
         std::int32_t* row = host_buf_ + b * pitch;
         const std::uint32_t nblk = (context_lens[b] + tpb - 1) / tpb;
@@ -213,6 +217,7 @@ bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vecto
         host_buf_[B * pitch + b] = static_cast<std::int32_t>(context_lens[b]);
     }
     alloc.flush();  // queued copy-on-write copies and swap moves land first
+    alloc.order_reads(host_buf_, B * pitch);  // swap-ins still filling a frame of the batch
     cudaStream_t st = alloc.stream();
     cudaMemcpyAsync(dev_buf_, host_buf_, ints * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
     cudaEventRecord(static_cast<cudaEvent_t>(upload_event_), st);
@@ -262,6 +267,18 @@ bool PagedDecodeBatch::run_resident(const std::vector<CacheView>& views, const s
         return false;
     }
     alloc.flush();  // queued copy-on-write copies and swap moves land first
+    if (alloc.loads_in_flight()) {
+        // only then: the frames of the batch against swap-ins still landing
+        std::vector<std::int32_t> frames;
+        const std::uint32_t tpb = alloc.block_shape().tokens_per_block;
+        for (std::size_t b = 0; b < views.size(); ++b) {
+            const std::uint32_t nblk = (context_lens[b] + tpb - 1) / tpb;
+            const std::size_t at = frames.size();
+            frames.resize(at + nblk);
+            if (!write_row(views[b], nblk, frames.data() + at)) frames.resize(at);
+        }
+        alloc.order_reads(frames.data(), frames.size());
+    }
     a.workspace = ws ? workspace_ : nullptr;
     a.workspace_bytes = ws ? workspace_bytes_ : 0;
     a.error_word = error_word_;

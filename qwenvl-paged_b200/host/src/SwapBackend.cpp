@@ -1,6 +1,7 @@
 #include "qwenvl_paged/SwapBackend.h"
 
 #include "qwenvl_paged/MemoryAllocator.h"
+#include "host_impl.h"
 #include "qvp.h"
 
 #include <cuda_runtime.h>
@@ -53,19 +54,31 @@ namespace {
 
 constexpr std::size_t kMaxStagingBytes = std::size_t(256) << 20;
 
-struct OnDevice {
-    int prev = -1;
-    bool switched = false;
-    explicit OnDevice(int device) {
-        if (device >= 0 && cudaGetDevice(&prev) == cudaSuccess && prev != device &&
-            cudaSetDevice(device) == cudaSuccess)
-            switched = true;
+using host_impl::OnDevice;
+
+cudaEvent_t ev(CUevent_st* e) { return reinterpret_cast<cudaEvent_t>(e); }
+
+bool make_event(CUevent_st*& e) {
+    cudaEvent_t x = nullptr;
+    if (cudaEventCreateWithFlags(&x, cudaEventDisableTiming) != cudaSuccess) {
         cudaGetLastError();
+        return false;
     }
-    ~OnDevice() {
-        if (switched) cudaSetDevice(prev);
+    e = reinterpret_cast<CUevent_st*>(x);
+    return true;
+}
+
+// Calls fn(first, count) for each maximal run of consecutive slab indices.
+template <typename Fn>
+void for_each_run(const std::uint32_t* idx, std::size_t n, Fn fn) {
+    std::size_t i = 0;
+    while (i < n) {
+        std::size_t j = i + 1;
+        while (j < n && idx[j] == idx[j - 1] + 1) ++j;
+        fn(i, j - i);
+        i = j;
     }
-};
+}
 
 }  // namespace
 
@@ -75,23 +88,48 @@ DeviceSwapBackend::DeviceSwapBackend(MemoryAllocator& allocator, std::size_t max
     slot_bytes_ = b0 != nullptr ? b0->size_bytes() : 0;
     if (!allocator.has_storage() || slot_bytes_ == 0 || max_slots_ == 0) return;
     OnDevice guard(allocator.device());
+    // Everything a flush needs is allocated here, so recorded moves always run.
+    const std::size_t staging = std::min<std::size_t>(
+        max_slots_, std::min<std::size_t>(65535, std::max<std::size_t>(1, kMaxStagingBytes / slot_bytes_)));
+    const std::size_t id_entries = 2 * max_slots_;
     void* p = nullptr;
-    if (cudaHostAlloc(&p, max_slots_ * slot_bytes_, cudaHostAllocDefault) != cudaSuccess) {
+    bool ok = cudaHostAlloc(&p, max_slots_ * slot_bytes_, cudaHostAllocDefault) == cudaSuccess;
+    if (ok) slab_ = static_cast<std::byte*>(p);
+    ok = ok && cudaMalloc(reinterpret_cast<void**>(&staging_), staging * slot_bytes_) == cudaSuccess;
+    for (int b = 0; ok && b < 2; ++b) {
+        ok = cudaMallocHost(reinterpret_cast<void**>(&ids_host_[b]), id_entries * sizeof(std::int32_t)) ==
+                 cudaSuccess &&
+             cudaMalloc(reinterpret_cast<void**>(&ids_dev_[b]), id_entries * sizeof(std::int32_t)) == cudaSuccess &&
+             make_event(ids_uploaded_[b]);
+    }
+    cudaStream_t cs = nullptr;
+    ok = ok && cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking) == cudaSuccess;
+    if (ok) copy_ = cs;
+    ok = ok && make_event(engine_mark_) && make_event(moves_done_);
+    if (!ok) {
         cudaGetLastError();
+        note("swap backend: a buffer, stream or event could not be allocated; every store is refused");
+        if (slab_ != nullptr) cudaFreeHost(slab_);
+        slab_ = nullptr;
         return;
     }
-    slab_ = static_cast<std::byte*>(p);
+    staging_blocks_ = staging;
     for (std::uint32_t i = 0; i < max_slots_; ++i) free_indices_.insert(free_indices_.end(), i);
 }
 
 DeviceSwapBackend::~DeviceSwapBackend() {
     OnDevice guard(allocator_->device());
-    cudaStreamSynchronize(allocator_->stream());
+    if (copy_ != nullptr) host_impl::wait_stream(copy_, "swap backend teardown", nullptr);
     if (slab_ != nullptr) cudaFreeHost(slab_);
     if (staging_ != nullptr) cudaFree(staging_);
-    if (ids_dev_ != nullptr) cudaFree(ids_dev_);
-    if (ids_host_ != nullptr) cudaFreeHost(ids_host_);
-    if (ids_event_ != nullptr) cudaEventDestroy(static_cast<cudaEvent_t>(ids_event_));
+    for (int b = 0; b < 2; ++b) {
+        if (ids_dev_[b] != nullptr) cudaFree(ids_dev_[b]);
+        if (ids_host_[b] != nullptr) cudaFreeHost(ids_host_[b]);
+        if (ids_uploaded_[b] != nullptr) cudaEventDestroy(ev(ids_uploaded_[b]));
+    }
+    if (engine_mark_ != nullptr) cudaEventDestroy(ev(engine_mark_));
+    if (moves_done_ != nullptr) cudaEventDestroy(ev(moves_done_));
+    if (copy_ != nullptr) cudaStreamDestroy(copy_);
 }
 
 void DeviceSwapBackend::note(const std::string& what) {
@@ -115,7 +153,7 @@ std::optional<SwapSlotId> DeviceSwapBackend::store(const PhysicalBlock& block) {
     if (free_indices_.empty()) return std::nullopt;
     if (block.data() != allocator_->pool_base() + static_cast<std::size_t>(block.id()) * allocator_->block_stride())
         return std::nullopt;  // not a block of this backend's pool
-    if (!pending_loads_.empty()) flush_loads();
+    if (!pending_loads_.empty()) flush();  // stores and loads keep their program order
     const std::uint32_t idx = *free_indices_.begin();
     free_indices_.erase(free_indices_.begin());
     const SwapSlotId slot = next_slot_++;
@@ -129,7 +167,7 @@ bool DeviceSwapBackend::load(SwapSlotId slot, PhysicalBlock& block) {
     if (it == slots_.end() || block.size_bytes() < slot_bytes_) return false;
     if (block.data() != allocator_->pool_base() + static_cast<std::size_t>(block.id()) * allocator_->block_stride())
         return false;
-    if (!pending_stores_.empty()) flush_stores();
+    if (!pending_stores_.empty()) flush();
     pending_loads_.push_back({static_cast<std::int32_t>(block.id()), it->second});
     return true;
 }
@@ -146,122 +184,112 @@ void DeviceSwapBackend::discard(SwapSlotId slot) {
 }
 
 void DeviceSwapBackend::flush() {
-    flush_stores();
-    flush_loads();
+    if (pending_stores_.empty() && pending_loads_.empty()) {
+        for (std::uint32_t idx : release_after_flush_) free_indices_.insert(idx);
+        release_after_flush_.clear();
+        return;
+    }
+    OnDevice guard(allocator_->device());
+    // The moves follow every piece of engine work already enqueued (earlier
+    // writes into a stored frame, earlier reads of a frame a load refills).
+    cudaEventRecord(ev(engine_mark_), allocator_->stream());
+    cudaStreamWaitEvent(copy_, ev(engine_mark_), 0);
+    // one upload of the whole block-id list, into the list not used by the
+    // previous flush (whose upload is long done unless flushes run back to back)
+    const int b = ids_next_;
+    ids_next_ ^= 1;
+    if (!host_impl::wait_event(ev(ids_uploaded_[b]), "swap flush: id list still uploading", &error_)) return;
+    std::size_t n = 0;
+    for (const Move& m : pending_stores_) ids_host_[b][n++] = m.block;
+    for (const Move& m : pending_loads_) ids_host_[b][n++] = m.block;
+    cudaMemcpyAsync(ids_dev_[b], ids_host_[b], n * sizeof(std::int32_t), cudaMemcpyHostToDevice, copy_);
+    cudaEventRecord(ev(ids_uploaded_[b]), copy_);
+    ++flush_seq_;
+    const bool loads = !pending_loads_.empty();
+    flush_moves(pending_stores_, true, ids_dev_[b]);
+    flush_moves(pending_loads_, false, ids_dev_[b] + (n - pending_loads_.size()));
+    cudaEventRecord(ev(moves_done_), copy_);
+    if (loads) last_load_flush_ = flush_seq_;
+    pending_stores_.clear();
+    pending_loads_.clear();
     for (std::uint32_t idx : release_after_flush_) free_indices_.insert(idx);
     release_after_flush_.clear();
 }
 
-bool DeviceSwapBackend::ensure_staging(std::size_t blocks) {
-    // one gather/scatter launch moves at most 65535 blocks
-    const std::size_t cap = std::min<std::size_t>(65535, std::max<std::size_t>(1, kMaxStagingBytes / slot_bytes_));
-    const std::size_t want = std::min(blocks, cap);
-    if (want <= staging_blocks_ && ids_capacity_ >= want) return true;
-    cudaStreamSynchronize(allocator_->stream());
-    if (staging_ != nullptr) cudaFree(staging_);
-    if (ids_dev_ != nullptr) cudaFree(ids_dev_);
-    if (ids_host_ != nullptr) cudaFreeHost(ids_host_);
-    staging_ = nullptr;
-    ids_dev_ = nullptr;
-    ids_host_ = nullptr;
-    staging_blocks_ = ids_capacity_ = 0;
-    if (cudaMalloc(reinterpret_cast<void**>(&staging_), want * slot_bytes_) != cudaSuccess ||
-        cudaMalloc(reinterpret_cast<void**>(&ids_dev_), want * sizeof(std::int32_t)) != cudaSuccess ||
-        cudaMallocHost(reinterpret_cast<void**>(&ids_host_), want * sizeof(std::int32_t)) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
+// Enqueues `moves` on the copy stream in chunks of the staging size; ids_dev
+// already holds their block ids in order.
+void DeviceSwapBackend::flush_moves(std::vector<Move>& moves, bool stores, std::int32_t* ids_dev) {
+    if (moves.empty()) return;
+    std::vector<std::uint32_t> idx(moves.size());
+    for (std::size_t i = 0; i < moves.size(); ++i) idx[i] = moves[i].slab_index;
+    if (!stores) {
+        if (frame_load_flush_.size() < allocator_->num_blocks()) frame_load_flush_.resize(allocator_->num_blocks(), 0);
+        for (const Move& m : moves) frame_load_flush_[static_cast<std::size_t>(m.block)] = flush_seq_;
     }
-    if (ids_event_ == nullptr) {
-        cudaEvent_t ev = nullptr;
-        if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
-            cudaGetLastError();
-            return false;
+    for (std::size_t base = 0; base < moves.size(); base += staging_blocks_) {
+        const std::size_t n = std::min(staging_blocks_, moves.size() - base);
+        if (stores) {
+            if (qvp_gather_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(),
+                                  slot_bytes_, ids_dev + base, static_cast<std::uint32_t>(n), staging_, nullptr,
+                                  copy_) != QVP_OK)
+                note(std::string("swap-out gather: ") + qvp_last_error());
+            for_each_run(idx.data() + base, n, [&](std::size_t first, std::size_t count) {
+                cudaMemcpyAsync(slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
+                                staging_ + first * slot_bytes_, count * slot_bytes_, cudaMemcpyDeviceToHost, copy_);
+            });
+            bytes_out_ += n * slot_bytes_;
+        } else {
+            for_each_run(idx.data() + base, n, [&](std::size_t first, std::size_t count) {
+                cudaMemcpyAsync(staging_ + first * slot_bytes_,
+                                slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
+                                count * slot_bytes_, cudaMemcpyHostToDevice, copy_);
+            });
+            if (qvp_scatter_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(),
+                                   slot_bytes_, ids_dev + base, static_cast<std::uint32_t>(n), staging_, nullptr,
+                                   copy_) != QVP_OK)
+                note(std::string("swap-in scatter: ") + qvp_last_error());
+            bytes_in_ += n * slot_bytes_;
         }
-        ids_event_ = ev;
-    }
-    staging_blocks_ = ids_capacity_ = want;
-    return true;
-}
-
-namespace {
-
-// Calls fn(first, count) for each maximal run of consecutive slab indices.
-template <typename Fn>
-void for_each_run(const std::uint32_t* idx, std::size_t n, Fn fn) {
-    std::size_t i = 0;
-    while (i < n) {
-        std::size_t j = i + 1;
-        while (j < n && idx[j] == idx[j - 1] + 1) ++j;
-        fn(i, j - i);
-        i = j;
     }
 }
 
-}  // namespace
+void DeviceSwapBackend::refresh_loads() const {
+    if (done_seq_ < flush_seq_ && cudaEventQuery(ev(moves_done_)) == cudaSuccess) done_seq_ = flush_seq_;
+    cudaGetLastError();
+}
 
-void DeviceSwapBackend::flush_stores() {
-    if (pending_stores_.empty()) return;
+bool DeviceSwapBackend::loads_in_flight() const {
+    if (last_load_flush_ <= std::max(done_seq_, engine_waited_)) return false;
+    refresh_loads();
+    return last_load_flush_ > std::max(done_seq_, engine_waited_);
+}
+
+void DeviceSwapBackend::order_engine(CUstream_st* engine, const std::int32_t* frames, std::size_t n, bool writes) {
+    if (flush_seq_ <= engine_waited_) return;
+    refresh_loads();
+    const std::uint64_t settled = std::max(done_seq_, engine_waited_);
+    if (flush_seq_ <= settled) return;
+    const bool loads = last_load_flush_ > settled;
+    bool wait = writes || (frames == nullptr && loads);
+    if (!wait && loads && frames != nullptr) {
+        const std::size_t nf = frame_load_flush_.size();
+        for (std::size_t i = 0; i < n && !wait; ++i) {
+            const std::int32_t f = frames[i];
+            wait = f >= 0 && static_cast<std::size_t>(f) < nf && frame_load_flush_[static_cast<std::size_t>(f)] > settled;
+        }
+    }
+    if (!wait) return;
     OnDevice guard(allocator_->device());
-    cudaStream_t st = allocator_->stream();
-    if (!ensure_staging(pending_stores_.size())) {
-        // the frames were already handed back to the pool: their bytes are lost
-        note("swap-out: device staging could not be allocated; " + std::to_string(pending_stores_.size()) +
-             " stored blocks were not moved");
-        pending_stores_.clear();
-        return;
-    }
-    std::vector<std::uint32_t> idx(staging_blocks_);
-    for (std::size_t base = 0; base < pending_stores_.size(); base += staging_blocks_) {
-        const std::size_t n = std::min(staging_blocks_, pending_stores_.size() - base);
-        cudaEventSynchronize(static_cast<cudaEvent_t>(ids_event_));
-        for (std::size_t i = 0; i < n; ++i) {
-            ids_host_[i] = pending_stores_[base + i].block;
-            idx[i] = pending_stores_[base + i].slab_index;
-        }
-        cudaMemcpyAsync(ids_dev_, ids_host_, n * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
-        cudaEventRecord(static_cast<cudaEvent_t>(ids_event_), st);
-        if (qvp_gather_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(), slot_bytes_,
-                              ids_dev_, static_cast<std::uint32_t>(n), staging_, nullptr, st) != QVP_OK)
-            note(std::string("swap-out gather: ") + qvp_last_error());
-        for_each_run(idx.data(), n, [&](std::size_t first, std::size_t count) {
-            cudaMemcpyAsync(slab_ + static_cast<std::size_t>(idx[first]) * slot_bytes_, staging_ + first * slot_bytes_,
-                            count * slot_bytes_, cudaMemcpyDeviceToHost, st);
-        });
-        bytes_out_ += n * slot_bytes_;
-    }
-    pending_stores_.clear();
+    cudaStreamWaitEvent(engine, ev(moves_done_), 0);
+    engine_waited_ = flush_seq_;
 }
 
-void DeviceSwapBackend::flush_loads() {
-    if (pending_loads_.empty()) return;
+bool DeviceSwapBackend::wait_idle() {
+    if (copy_ == nullptr) return error_.empty();
     OnDevice guard(allocator_->device());
-    cudaStream_t st = allocator_->stream();
-    if (!ensure_staging(pending_loads_.size())) {
-        note("swap-in: device staging could not be allocated; " + std::to_string(pending_loads_.size()) +
-             " loaded blocks were not restored");
-        pending_loads_.clear();
-        return;
-    }
-    std::vector<std::uint32_t> idx(staging_blocks_);
-    for (std::size_t base = 0; base < pending_loads_.size(); base += staging_blocks_) {
-        const std::size_t n = std::min(staging_blocks_, pending_loads_.size() - base);
-        cudaEventSynchronize(static_cast<cudaEvent_t>(ids_event_));
-        for (std::size_t i = 0; i < n; ++i) {
-            ids_host_[i] = pending_loads_[base + i].block;
-            idx[i] = pending_loads_[base + i].slab_index;
-        }
-        for_each_run(idx.data(), n, [&](std::size_t first, std::size_t count) {
-            cudaMemcpyAsync(staging_ + first * slot_bytes_, slab_ + static_cast<std::size_t>(idx[first]) * slot_bytes_,
-                            count * slot_bytes_, cudaMemcpyHostToDevice, st);
-        });
-        cudaMemcpyAsync(ids_dev_, ids_host_, n * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
-        cudaEventRecord(static_cast<cudaEvent_t>(ids_event_), st);
-        if (qvp_scatter_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(), slot_bytes_,
-                               ids_dev_, static_cast<std::uint32_t>(n), staging_, nullptr, st) != QVP_OK)
-            note(std::string("swap-in scatter: ") + qvp_last_error());
-        bytes_in_ += n * slot_bytes_;
-    }
-    pending_loads_.clear();
+    const bool ok = host_impl::wait_stream(copy_, "swap moves", &error_);
+    if (ok) done_seq_ = flush_seq_;
+    return ok && error_.empty();
 }
 
 }  // namespace qwenvl_paged

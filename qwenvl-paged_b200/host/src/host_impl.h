@@ -10,9 +10,12 @@
 
 #include <cuda_runtime.h>
 
+#include <chrono>
 #include <cstddef>
 #include <cstdint>
 #include <optional>
+#include <string>
+#include <thread>
 #include <vector>
 
 namespace qwenvl_paged {
@@ -31,6 +34,54 @@ struct OnDevice {
         if (switched) cudaSetDevice(prev);
     }
 };
+
+// How long a host-side wait for device work may last before it gives up
+// with an error (a healthy wait here is milliseconds; a device that stopped
+// answering must not hang the engine thread).
+constexpr double kHostWaitLimitSeconds = 60.0;
+
+// Polls `ev` until it completes; false (with `err` set) on a device error or
+// after kHostWaitLimitSeconds.
+inline bool wait_event(cudaEvent_t ev, const char* what, std::string* err) {
+    if (ev == nullptr) return true;
+    const auto start = std::chrono::steady_clock::now();
+    for (unsigned spins = 0;; ++spins) {
+        const cudaError_t e = cudaEventQuery(ev);
+        if (e == cudaSuccess) return true;
+        if (e != cudaErrorNotReady) {
+            cudaGetLastError();
+            if (err != nullptr && err->empty()) *err = std::string(what) + ": " + cudaGetErrorString(e);
+            return false;
+        }
+        if (spins > 64) {
+            if (std::chrono::duration<double>(std::chrono::steady_clock::now() - start).count() >
+                kHostWaitLimitSeconds) {
+                if (err != nullptr && err->empty()) *err = std::string(what) + ": timed out";
+                return false;
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(spins > 1024 ? 200 : 20));
+        }
+    }
+}
+
+// Waits (bounded, as wait_event) for everything enqueued on `stream` so far.
+inline bool wait_stream(cudaStream_t stream, const char* what, std::string* err) {
+    cudaEvent_t ev = nullptr;
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) != cudaSuccess) {
+        cudaGetLastError();
+        if (err != nullptr && err->empty()) *err = std::string(what) + ": could not create an event";
+        return false;
+    }
+    bool ok = cudaEventRecord(ev, stream) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        if (err != nullptr && err->empty()) *err = std::string(what) + ": could not record an event";
+    } else {
+        ok = wait_event(ev, what, err);
+    }
+    cudaEventDestroy(ev);
+    return ok;
+}
 
 inline bool is_device_pointer(const void* p) {
     cudaPointerAttributes a{};

@@ -275,12 +275,14 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
     std::uint64_t swapped = 0;
     for (std::size_t i : pre) swapped += cache.swap_out_sequence(seqs[i]);
     const double out_host_s = now_s() - h0;
+    // the moves run on the backend's copy stream, after the engine's work
+    cudaStream_t cs = swap.copy_stream();
     cudaEventRecord(ev.a, alloc.stream());
     const double f0 = now_s();
     alloc.flush();
-    cudaEventRecord(ev.b, alloc.stream());
-    const double out_ms = ev.ms();
     const double out_wall = now_s() - f0;
+    cudaEventRecord(ev.b, cs);
+    const double out_ms = ev.ms();
     // a decode step while the swapped quarter is away
     refresh();
     batch.run(views, bctx, 0, hq, 0.0884f, q, o);
@@ -291,7 +293,7 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
     const double in_host_s = now_s() - h1;
     cudaEventRecord(ev.a, alloc.stream());
     alloc.flush();
-    cudaEventRecord(ev.b, alloc.stream());
+    cudaEventRecord(ev.b, cs);
     const double in_ms = ev.ms();
     // decode stall: a step over resumed sequences issued right after their
     // swap-in waits for it on the stream; measure issue -> done
@@ -320,9 +322,40 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
         cudaEventRecord(ev.a, alloc.stream());
         for (int b = 0; b < R; ++b) cache.swap_in_sequence(seqs[pre[b]]);
         for (int b = 0; b < R; ++b) rviews[b] = *cache.cache_view(seqs[pre[b]]);
-        dec_ok = batch.run(rviews, rctx, 0, hq, 0.0884f, q, o);  // flushes the swap-in first
+        dec_ok = batch.run(rviews, rctx, 0, hq, 0.0884f, q, o);  // waits for the swap-in of its frames
         cudaEventRecord(ev.b, alloc.stream());
         stall_ms = ev.ms() - rdecode_ms;
+    }
+    // Decode of the resident batch while the resumed batch moves over PCIe on
+    // the copy stream: first while it swaps out, then while it swaps in. The
+    // resident batch reads no frame being moved, so it need not wait.
+    float overlap_out_ms = 0.f, overlap_in_ms = 0.f;
+    bool out_still_moving = false, in_still_moving = false;
+    if (!rviews.empty()) {
+        const int R = static_cast<int>(rviews.size());
+        cudaEvent_t moved_ev;
+        cudaEventCreateWithFlags(&moved_ev, cudaEventDisableTiming);
+        alloc.synchronize();
+        for (int b = 0; b < R; ++b) cache.swap_out_sequence(seqs[pre[b]]);
+        alloc.flush();
+        cudaEventRecord(moved_ev, cs);
+        cudaEventRecord(ev.a, alloc.stream());
+        dec_ok = batch.run(views, bctx, 0, hq, 0.0884f, q, o) && dec_ok;
+        cudaEventRecord(ev.b, alloc.stream());
+        overlap_out_ms = ev.ms();
+        out_still_moving = cudaEventQuery(moved_ev) == cudaErrorNotReady;
+        alloc.synchronize();
+        for (int b = 0; b < R; ++b) cache.swap_in_sequence(seqs[pre[b]]);
+        alloc.flush();
+        cudaEventRecord(moved_ev, cs);
+        cudaEventRecord(ev.a, alloc.stream());
+        dec_ok = batch.run(views, bctx, 0, hq, 0.0884f, q, o) && dec_ok;
+        cudaEventRecord(ev.b, alloc.stream());
+        overlap_in_ms = ev.ms();
+        in_still_moving = cudaEventQuery(moved_ev) == cudaErrorNotReady;
+        cudaGetLastError();
+        alloc.synchronize();
+        cudaEventDestroy(moved_ev);
     }
     const int derr = batch.device_error();
     cudaFree(q);
@@ -338,7 +371,12 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
        << ", \"swap_in_host_bookkeeping_ms\": " << in_host_s * 1e3 << ", \"all_resumed\": "
        << (all_in ? "true" : "false") << ", \"pcie_d2h_peak_gbs\": " << d2h_peak << ", \"pcie_h2d_peak_gbs\": "
        << h2d_peak << ", \"decode_batch\": " << B << ", \"decode_ms\": " << decode_ms
-       << ", \"resume_batch_decode_ms\": " << rdecode_ms << ", \"resume_batch_stall_ms\": " << stall_ms << ", \"resume_batch_sequences\": " << rviews.size()
+       << ", \"resume_batch_decode_ms\": " << rdecode_ms << ", \"resume_batch_stall_ms\": " << stall_ms
+       << ", \"resume_batch_sequences\": " << rviews.size()
+       << ", \"resident_decode_during_swap_out_ms\": " << overlap_out_ms
+       << ", \"swap_out_still_moving_after_that_decode\": " << (out_still_moving ? "true" : "false")
+       << ", \"resident_decode_during_swap_in_ms\": " << overlap_in_ms
+       << ", \"swap_in_still_moving_after_that_decode\": " << (in_still_moving ? "true" : "false")
        << ", \"pool_alloc_s\": " << pool_s << ", \"slab_pin_s\": " << pin_s << ", \"decode_ok\": "
        << (dec_ok ? "true" : "false") << ", \"decode_device_error\": " << derr << "}";
     return emit(js.str(), out, cap);

@@ -415,6 +415,38 @@ NATIVE_TEST(eviction_policy_advice_drives_a_swap_out_that_frees_the_block) {
     CHECK(e.alloc.info(*victim)->state == BlockState::Free);
 }
 
+// A swap backend whose buffers could not be allocated refuses every store
+// up front, so a swap-out changes nothing: no frame is freed, no generation
+// moves, the table keeps its mappings (the moves that were recorded are
+// never dropped later, because nothing is recorded).
+NATIVE_TEST(a_swap_backend_without_buffers_refuses_before_the_bookkeeping_moves) {
+    MemoryAllocator alloc(config(8), DevicePoolOptions{-1, false, nullptr});
+    DeviceSwapBackend swap(alloc, 4);  // no device storage: its buffers are never allocated
+    CHECK(!swap.ready());
+    alloc.set_swap_backend(&swap);
+    KVCacheManager cache(alloc);
+    CHECK(cache.create_sequence(meta(1)) && cache.reserve_tokens(1, 40));
+    std::vector<PhysicalBlockInfo> before;
+    for (PhysicalBlockId i = 0; i < 8; ++i) before.push_back(*alloc.info(i));
+    const std::vector<BlockTableEntry> table_before = cache.cache_view(1)->block_table->entries();
+    const AllocatorStats st_before = alloc.stats();
+    CHECK(cache.swap_out_sequence(1) == 0u);
+    CHECK(!alloc.swap_out(*cache.cache_view(1)->block_table->lookup(0)).has_value());
+    for (PhysicalBlockId i = 0; i < 8; ++i) {
+        CHECK(alloc.info(i)->state == before[i].state && alloc.info(i)->ref_count == before[i].ref_count &&
+              alloc.info(i)->generation == before[i].generation);
+    }
+    const std::vector<BlockTableEntry>& after = cache.cache_view(1)->block_table->entries();
+    CHECK(after.size() == table_before.size());
+    for (std::size_t i = 0; i < after.size(); ++i)
+        CHECK(after[i].physical_id == table_before[i].physical_id && !after[i].swap_slot.has_value());
+    CHECK(alloc.stats().free_blocks == st_before.free_blocks && alloc.stats().swapped_blocks == 0u);
+    // with nothing deferred, every ordering call is a no-op
+    CHECK(!alloc.loads_in_flight());
+    alloc.order_reads(nullptr, 0);
+    alloc.order_writes();
+}
+
 }  // namespace
 
 extern "C" __attribute__((visibility("default"))) int qvp_tablecases_list(char* out, size_t cap) {

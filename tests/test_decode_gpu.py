@@ -166,6 +166,9 @@ def test_decode_is_deterministic_across_calls():
     dict(batch=7, ctx_lo=1, ctx_hi=2000, hq=16, hkv=2, head_dim=64),
     dict(batch=5, ctx_lo=50, ctx_hi=900, hq=8, hkv=1, head_dim=128),
     dict(batch=6, ctx_lo=50, ctx_hi=900, hq=6, hkv=3, head_dim=128),
+    dict(batch=40, ctx_lo=1, ctx_hi=3000, hq=64, hkv=4, head_dim=128),   # G = 16: 8 outputs per merging thread
+    dict(batch=20, ctx_lo=300, ctx_hi=5000, hq=32, hkv=2, head_dim=64),  # two heads per CTA, G = 16
+    dict(batch=2, ctx_lo=30000, ctx_hi=40000, hq=7, hkv=1, head_dim=128),  # one head: hundreds of parts per merge
 ])
 def test_stream_k_matches_the_oracle(kw):
     w = W.small(20 + kw["batch"] + kw["hkv"], dtype="bf16", **kw)
@@ -173,8 +176,8 @@ def test_stream_k_matches_the_oracle(kw):
     assert plan["stream"], plan
 
 
-def test_stream_k_falls_back_to_the_grid_kernel_past_4096_segments():
-    w = W.small(21, batch=4100, ctx_lo=1, ctx_hi=20, hq=28, hkv=4, head_dim=128, dtype="bf16")
+def test_stream_k_falls_back_to_the_grid_kernel_past_2048_segments():
+    w = W.small(21, batch=2100, ctx_lo=1, ctx_hi=20, hq=28, hkv=4, head_dim=128, dtype="bf16")
     out, ref, plan = check(w)
     assert plan["fast"] and not plan["stream"]
 

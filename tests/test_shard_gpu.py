@@ -116,7 +116,8 @@ def test_one_shard_decode_is_qvp_decode_bit_for_bit():
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.full((w.batch, w.num_query_heads, w.head_dim), -3.0, dtype=torch.bfloat16, device=dev)
     keep = []
-    a = _decode_args(sw, pool_d, q_d, 0, tab_d, ctx_d, err)
+    # decode.out only has to be non-null: the shard decode writes the gather buffer
+    a = _decode_args(sw, pool_d, q_d, out.data_ptr(), tab_d, ctx_d, err)
     _with_workspace(a, dev, keep)
     sa = qvp.shard_decode_args(a, 0, 1, 0, None, 0, out.data_ptr())
     gathered = torch.empty(qvp.shard_gather_bytes(sa), dtype=torch.uint8, device=dev)
@@ -177,7 +178,7 @@ def _rank_main(rank, world, uid_path, result):
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     out = torch.zeros((w.batch, w.num_query_heads, w.head_dim), dtype=torch.bfloat16, device=dev)
     keep = []
-    a = _decode_args(sw, pool_d, q_d, 0, tab_d, ctx_d, err)
+    a = _decode_args(sw, pool_d, q_d, out.data_ptr(), tab_d, ctx_d, err)
     _with_workspace(a, dev, keep)
     sa = qvp.shard_decode_args(a, rank, world, rank, comm, 0, out.data_ptr())
     gathered = torch.empty(qvp.shard_gather_bytes(sa), dtype=torch.uint8, device=dev)
