@@ -326,6 +326,9 @@ __global__ void __launch_bounds__(kFastThreads, 1)
                 const float e1 = (mj1 == -INFINITY) ? 0.f : exp2f(mj1 - M1);
 #pragma unroll
                 for (int n = 0; n < NT; ++n) {
+                    // keep the loads next to their use (a full hoist would
+                    // hold 2 * NT more registers than the kernel has)
+                    asm volatile("" ::: "memory");
                     const int col = n * 8 + c * 2;
                     const float2 lo = *reinterpret_cast<const float2*>(w + g * D + col);
                     const float2 hi = *reinterpret_cast<const float2*>(w + (g + 8) * D + col);
@@ -377,29 +380,39 @@ __global__ void __launch_bounds__(kFastThreads, 1)
 // A "segment" is one (sequence, head group) pair; its blocks are cut into
 // stages of J blocks (the last stage of a segment may be short). All stages of
 // all segments, in sequence order, form one stream that is split evenly over
-// a grid of one CTA per SM: CTA c owns stages [c*S/grid, (c+1)*S/grid). The
-// producer warp walks that range streaming K/V with TMA, crossing segment
-// boundaries without a pause; every consumer warp keeps one running (max, sum,
-// accumulator) per segment piece and writes it as a partial record when the
-// piece ends. Records of segment sigma written by CTA c live at index
-// sigma + c, which is injective because segments and CTA ranges are both
-// contiguous in stage order. The CTA that completes the last piece of a
-// segment merges its records into the output (merge_segment): every CTA
-// counts its finished pieces on a per-segment arrival counter, and the one
-// whose arrival completes the count merges the segment once its own stream
-// is done (so the merge never stalls the pipeline). No CTA ever waits for
-// another, so the kernel needs no co-resident grid. The counters live in the
-// workspace, which may hold anything on entry: each holds (epoch << 32 |
-// count), and a word from another epoch (another call) counts as zero.
+// a grid of one CTA per SM: CTA c owns stages [c*S/grid, (c+1)*S/grid).
+//
+// A CTA's range holds at most two "shared" pieces (the segment it starts
+// inside, shared with the CTAs before it, and the one it ends inside, shared
+// with the CTAs after it) and any number of segments wholly its own. It
+// streams the shared pieces first (the one at its end, then the one at its
+// start) and its own segments after them, so every segment split between
+// CTAs has all its pieces done early in the kernel, and the kernel ends on
+// segments that need no merging. At the end of each piece the J warp columns
+// that share a kv head are combined in shared memory (a tree of log2 J
+// rounds); a segment wholly inside the CTA then writes its output directly,
+// while a shared piece writes one partial record per kv head at index
+// (segment + CTA) * HH + head (injective: segments and CTA ranges are both
+// contiguous in stage order) and counts itself on the segment's arrival
+// counter. The CTA whose piece completes the count merges the segment's
+// records into the output right away (merge_records), while its producer warp
+// keeps streaming. No CTA ever waits for another, so the kernel needs no
+// co-resident grid. The counters live in the workspace, which may hold
+// anything on entry: each holds (epoch << 32 | count), and a word from
+// another epoch (another call) counts as zero.
 
 constexpr int kStreamMaxSegments = 2048;
 
+// Fixed work of a segment, in stages, for 1, 2 and 4 kv heads per CTA
+// (per-CTA timings on cfg2-shaped batches: a piece's epilogue costs about
+// four stages at 4 heads per CTA; these values minimised the step time).
+constexpr uint32_t kSegmentCostStages[3] = {2u, 3u, 5u};
 
 struct StreamParams {
     const int32_t* tables;
     const int32_t* ctx;
     const __nv_bfloat16* q;
-    float* rec_acc;       // [records][G][D]
+    float* rec_acc;       // [records][G][D], records = (nseg + grid) * HH
     float2* rec_ml;       // [records][G]
     unsigned long long* seg_count;  // [nseg] arrival counters (epoch << 32 | pieces)
     __nv_bfloat16* out;   // [batch][hq][D]
@@ -413,8 +426,29 @@ struct StreamParams {
     uint32_t head_groups;  // z = kv heads / HH
     uint32_t nseg;         // batch * z
     uint32_t epoch;        // differs between calls
+    uint32_t seg_cost;     // fixed work of a segment, in stages (StreamSplit)
     float scale_log2;
 };
+
+// Floats of the per-CTA scratch that combines the J warp columns of a kv
+// head (and later holds a merge's weights): HH * J / 2 states of G rows.
+__host__ __device__ constexpr uint32_t stream_scratch_floats(uint32_t G, uint32_t D) {
+    return 4u * (G * D + 2u * G);  // HH * J = 8 warps, half of them write per round
+}
+
+// Dynamic shared memory of the stream kernel: the pipeline (3 stages of
+// 512 * head_dim bytes at head_dim 128, 6 at 64: 192 KiB either way, plus
+// alignment slack and barriers), the segment prefix and the scratch.
+constexpr uint32_t stream_pipeline_smem(uint32_t D) {
+    return 196608u + 1024u + 2u * (D == 64 ? 6u : 3u) * 8u + 16u;
+}
+// 227 KB per block on sm_100, less 1 KB kept for the kernel's static shared
+// memory (528 bytes)
+constexpr uint32_t kMaxDynamicSmem = 232448u - 1024u;
+constexpr size_t stream_smem_bytes(uint32_t nseg, uint32_t G, uint32_t D) {
+    return stream_pipeline_smem(D) + (static_cast<size_t>(nseg) + 1u) * 4u + 16u +
+           static_cast<size_t>(stream_scratch_floats(G, D)) * 4u;
+}
 
 __device__ __forceinline__ void grid_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -422,12 +456,6 @@ __device__ __forceinline__ void grid_launch_dependents() {
 
 __device__ __forceinline__ void grid_dependency_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
-}
-
-// True when CTA `cta` of a `grid`-CTA stream-K launch over `total` stages
-// got an empty range (possible when total < grid); such a CTA wrote nothing.
-__device__ __forceinline__ bool cta_is_empty(uint32_t cta, uint32_t total, uint32_t grid) {
-    return static_cast<uint64_t>(cta) * total / grid == static_cast<uint64_t>(cta + 1) * total / grid;
 }
 
 // Largest sigma in [0, nseg) with prefix[sigma] <= x (prefix non-decreasing).
@@ -443,14 +471,49 @@ __device__ __forceinline__ int find_segment(const int32_t* prefix, int nseg, uin
     return lo;
 }
 
-// First and last CTA whose stage ranges intersect stages [ps, pe) (pe > ps)
-// of a `grid`-CTA stream-K launch over `total` stages: CTA c owns stages
-// [c*total/grid, (c+1)*total/grid).
-__device__ __forceinline__ void pieces_of(uint32_t ps, uint32_t pe, uint32_t total, uint32_t grid, uint32_t& cf,
-                                          uint32_t& cl) {
-    cf = static_cast<uint32_t>((static_cast<uint64_t>(ps + 1) * grid - 1) / total);
-    cl = static_cast<uint32_t>((static_cast<uint64_t>(pe) * grid - 1) / total);
-}
+// How the stage stream is cut into CTA ranges. Every segment costs its
+// stages plus `b` stage-equivalents of fixed work (its epilogue and, for a
+// piece shared between CTAs, the records and the merge), placed before its
+// stages; the total cost C is split evenly, so a CTA whose range holds more
+// segment starts gets fewer stages. Stage x of segment sg sits at cost
+// x + b * (sg + 1).
+struct StreamSplit {
+    const int32_t* prefix;  // [nseg + 1] stage prefix (shared memory)
+    int nseg;
+    uint32_t total, grid, b;
+    uint64_t cost;
+
+    // First stage at or after cost position y.
+    __device__ uint32_t stage_at(uint64_t y) const {
+        if (y >= cost) return total;
+        int lo = 0, hi = nseg - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (static_cast<uint64_t>(prefix[mid]) + static_cast<uint64_t>(b) * mid <= y)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        const uint64_t seg0 = static_cast<uint64_t>(prefix[lo]) + static_cast<uint64_t>(b) * lo + b;
+        const uint64_t x = static_cast<uint64_t>(prefix[lo]) + (y > seg0 ? y - seg0 : 0);
+        return static_cast<uint32_t>(min(x, static_cast<uint64_t>(prefix[lo + 1])));
+    }
+    __device__ uint32_t begin(uint32_t c) const { return stage_at(static_cast<uint64_t>(c) * cost / grid); }
+    __device__ bool empty(uint32_t c) const { return begin(c) == begin(c + 1); }
+    // The CTA whose range holds stage x of segment sg.
+    __device__ uint32_t cta_of(uint32_t x, int sg) const {
+        const uint64_t y = x + static_cast<uint64_t>(b) * (sg + 1);
+        return static_cast<uint32_t>(((y + 1) * grid - 1) / cost);
+    }
+    // First and last CTA holding a piece of (non-empty) segment sg.
+    __device__ void pieces(int sg, uint32_t& cf, uint32_t& cl) const {
+        cf = cta_of(static_cast<uint32_t>(prefix[sg]), sg);
+        cl = cta_of(static_cast<uint32_t>(prefix[sg + 1]) - 1u, sg);
+    }
+    // Whether some CTA may get an empty range (its share of the cost is no
+    // larger than one segment's fixed cost).
+    __device__ bool may_have_empty() const { return cost <= static_cast<uint64_t>(grid) * (b + 1); }
+};
 
 // Counts one finished piece of a segment on its arrival counter; true for the
 // arrival that completes `expected`. A word whose epoch is not `epoch` (left
@@ -469,145 +532,181 @@ __device__ __forceinline__ bool arrive_last(unsigned long long* counter, uint32_
     return done == expected;
 }
 
-// Merges every partial record of segment `sg` (its HH kv heads, G query rows
-// each) into the output; run after the CTA's stream by its kFastComputeWarps
-// consumer warps (tid < 256), with the pipeline's shared memory free. The
-// records of one CTA's piece are contiguous (HH * J of them), so thread 0
-// brings each piece into shared memory with two bulk copies (accumulators,
-// then maxima and sums); as many pieces as fit go in one round trip. Per
-// chunk of pieces: the running max and sum of every row (threads r < HH*G),
-// then each thread rescales its OPT float4 outputs and adds the chunk's parts
-// from shared memory. The order of summation depends on neither the CTA that
-// merges nor timing, so results are identical from call to call.
-template <int D, int HH, int J, int OPT>
-__device__ __forceinline__ bool merge_segment(const float* __restrict__ rec_acc, const float2* __restrict__ rec_ml,
+// The pieces of one CTA's stage range [x0, x1), in the order it streams
+// them: the shared piece at its end, the shared piece at its start, then the
+// segments wholly inside the range (empty segments are skipped by callers).
+struct PieceOrder {
+    int first, last;
+    uint32_t x0, x1;
+    bool head_shared, tail_shared;
+    int nshared, count;
+
+    __device__ PieceOrder(const int32_t* prefix, int nseg, uint32_t lo, uint32_t hi) : x0(lo), x1(hi) {
+        first = find_segment(prefix, nseg, lo);
+        last = find_segment(prefix, nseg, hi - 1);
+        head_shared = static_cast<uint32_t>(prefix[first]) < lo;
+        tail_shared = static_cast<uint32_t>(prefix[last + 1]) > hi;
+        if (first == last) {
+            nshared = 0;
+            count = 1;
+        } else {
+            nshared = (tail_shared ? 1 : 0) + (head_shared ? 1 : 0);
+            count = last - first + 1;
+        }
+    }
+
+    // Segment, stage range [b, e) and whether the segment lies wholly in
+    // this CTA, for piece i < count.
+    __device__ void at(const int32_t* prefix, int i, int& sg, uint32_t& b, uint32_t& e, bool& whole) const {
+        if (first == last) {
+            sg = first;
+            b = x0;
+            e = x1;
+            whole = !head_shared && !tail_shared;
+            return;
+        }
+        if (i < nshared) {
+            if (tail_shared && i == 0) {
+                sg = last;
+                b = static_cast<uint32_t>(prefix[last]);
+                e = x1;
+            } else {
+                sg = first;
+                b = x0;
+                e = static_cast<uint32_t>(prefix[first + 1]);
+            }
+            whole = false;
+            return;
+        }
+        sg = first + (head_shared ? 1 : 0) + (i - nshared);
+        b = static_cast<uint32_t>(prefix[sg]);
+        e = static_cast<uint32_t>(prefix[sg + 1]);
+        whole = true;
+    }
+};
+
+// Merges the partial records of segment `sg` (HH kv heads of G rows; one
+// record per head per piece) into the output. Run by the kFastComputeWarps
+// consumer warps (tid < 256) of the CTA whose piece completed the segment.
+// Pieces are the non-empty CTAs cf..cl. Per chunk of `chunk` pieces: (A)
+// every (piece, row) max and sum into shared memory in one parallel pass,
+// (B) per row the running max and sum; once all are in, (C) per chunk the
+// normalised weights in place of the maxima, then each thread sums its OPT
+// float4 outputs over the chunk, KU pieces' loads in flight at once. The
+// order of summation depends on neither the merging CTA nor timing.
+template <int D, int HH, int OPT>
+__device__ __noinline__ void merge_records(const float* __restrict__ rec_acc, const float2* __restrict__ rec_ml,
                                               __nv_bfloat16* __restrict__ out, uint32_t group, uint32_t head_groups,
-                                              uint32_t hq, int sg, uint32_t cf, uint32_t cl, uint32_t total,
-                                              uint32_t grid, uint8_t* stage, uint32_t stage_bytes, uint32_t bar,
-                                              uint32_t& phase, float* s_stat, int tid, int32_t* err) {
+                                              uint32_t hq, int sg, uint32_t cf, uint32_t cl, StreamSplit split,
+                                              float* s_wm, float* s_wl, int chunk, float* s_stat, int tid) {
     constexpr int D4 = D / 4;
     constexpr int kThreads = kFastComputeWarps * 32;
-    constexpr int kParts = HH * J;  // records per piece
+    constexpr int KU = OPT >= 8 ? 1 : 8 / OPT;
     const int G = static_cast<int>(group);
     const int R = HH * G;
-    const uint32_t acc_bytes = static_cast<uint32_t>(kParts * G * D) * 4u;
-    const uint32_t ml_bytes = static_cast<uint32_t>(kParts * G) * 8u;
-    const uint32_t piece_bytes = acc_bytes + ml_bytes;
-    const uint32_t per_chunk = stage_bytes / piece_bytes;  // >= 1 for every supported shape
-    float* s_max = s_stat;       // [R] running max
-    float* s_sum = s_stat + 64;  // [R] running sum
-    float* s_scale = s_stat + 128;  // [R] rescale of the running accumulators
-    if (tid < R) {
-        s_max[tid] = -INFINITY;
-        s_sum[tid] = 0.f;
+    const int nparts = static_cast<int>(cl - cf + 1);
+    const bool may_be_empty = split.may_have_empty();
+    auto rec_of = [&](int k, int hh) { return (static_cast<size_t>(sg) + cf + static_cast<uint32_t>(k)) * HH + hh; };
+    auto usable = [&](int k) { return !may_be_empty || !split.empty(cf + static_cast<uint32_t>(k)); };
+    auto load_stats = [&](int k0, int nk) {
+        for (int i = tid; i < nk * R; i += kThreads) {
+            const int kk = i / R, rr = i % R;
+            float2 ml = make_float2(-INFINITY, 0.f);
+            if (usable(k0 + kk)) ml = __ldcg(&rec_ml[rec_of(k0 + kk, rr / G) * G + rr % G]);
+            s_wm[i] = ml.x;
+            s_wl[i] = ml.y;
+        }
+    };
+    float* s_max = s_stat;
+    float* s_inv = s_stat + 64;
+
+    float run_m = -INFINITY, run_l = 0.f;  // thread rr < R
+    for (int k0 = 0; k0 < nparts; k0 += chunk) {
+        const int nk = min(chunk, nparts - k0);
+        load_stats(k0, nk);
+        named_barrier(1, kThreads);
+        if (tid < R) {
+            for (int kk = 0; kk < nk; ++kk) {
+                const float mk = s_wm[kk * R + tid];
+                if (mk == -INFINITY) continue;
+                const float mn = fmaxf(run_m, mk);
+                run_l = run_l * exp2f(run_m - mn) + s_wl[kk * R + tid] * exp2f(mk - mn);
+                run_m = mn;
+            }
+        }
+        named_barrier(1, kThreads);
     }
-    if (tid == 0) s_stat[192] = 0.f;  // wait-timeout vote
+    if (tid < R) {
+        s_max[tid] = run_m;
+        s_inv[tid] = 1.f / run_l;
+    }
     named_barrier(1, kThreads);
+
     const int nout = R * D4;
     float4 acc[OPT];
 #pragma unroll
     for (int i = 0; i < OPT; ++i) acc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-
-    uint32_t c = cf;
-    while (c <= cl) {
-        // this chunk: the next per_chunk non-empty CTAs of [c, cl]
-        uint32_t pieces[8];
-        uint32_t np = 0;
-        for (; c <= cl && np < per_chunk && np < 8; ++c)
-            if (!(total < grid && cta_is_empty(c, total, grid))) pieces[np++] = c;
-        if (np == 0) break;
-        if (tid == 0) {
-            // generic-proxy reads of this shared memory are done (barrier
-            // below) and the records were published to this thread (acquire)
-            asm volatile("fence.proxy.async;" ::: "memory");
-            mbar_arrive_expect_tx(bar, np * piece_bytes);
-            for (uint32_t i = 0; i < np; ++i) {
-                const size_t rec0 = (static_cast<size_t>(sg) + pieces[i]) * kParts;
-                const uint32_t dst = smem_u32(stage + i * piece_bytes);
-                bulk_load(dst, rec_acc + rec0 * G * D, acc_bytes, bar);
-                bulk_load(dst + acc_bytes, rec_ml + rec0 * G, ml_bytes, bar);
-            }
+    for (int k0 = 0; k0 < nparts; k0 += chunk) {
+        const int nk = min(chunk, nparts - k0);
+        if (nparts > chunk) {  // otherwise the only chunk's stats are still in shared memory
+            load_stats(k0, nk);
+            named_barrier(1, kThreads);
         }
-        // the verdict on the wait must be the same in every thread (they
-        // meet at named barriers below), so the threads vote on it
-        if (!mbar_wait_bounded(bar, phase)) s_stat[192] = 1.f;
-        named_barrier(1, kThreads);
-        if (s_stat[192] != 0.f) {
-            // give copies still in flight one more bounded wait, then stop
-            if (tid == 0) {
-                record_error(err, kErrWaitTimeout);
-                mbar_wait_bounded(bar, phase);
-            }
-            return false;
-        }
-        phase ^= 1u;
-        // running max / sum per row over this chunk's parts
-        if (tid < R) {
-            const int hh = tid / G, r = tid % G;
-            float m_old = s_max[tid], m_new = m_old;
-            for (uint32_t i = 0; i < np; ++i) {
-                const float2* ml = reinterpret_cast<const float2*>(stage + i * piece_bytes + acc_bytes);
-                for (int jj = 0; jj < J; ++jj) m_new = fmaxf(m_new, ml[(hh * J + jj) * G + r].x);
-            }
-            float l = m_old == -INFINITY ? 0.f : s_sum[tid] * exp2f(m_old - m_new);
-            for (uint32_t i = 0; i < np; ++i) {
-                const float2* ml = reinterpret_cast<const float2*>(stage + i * piece_bytes + acc_bytes);
-                for (int jj = 0; jj < J; ++jj) {
-                    const float2 v = ml[(hh * J + jj) * G + r];
-                    if (v.x != -INFINITY) l += v.y * exp2f(v.x - m_new);
-                }
-            }
-            s_scale[tid] = (m_old == -INFINITY) ? 0.f : exp2f(m_old - m_new);
-            s_max[tid] = m_new;
-            s_sum[tid] = l;
+        for (int i = tid; i < nk * R; i += kThreads) {
+            const float mk = s_wm[i];
+            const int rr = i % R;
+            s_wm[i] = mk == -INFINITY ? 0.f : exp2f(mk - s_max[rr]) * s_inv[rr];
         }
         named_barrier(1, kThreads);
+        for (int kk0 = 0; kk0 < nk; kk0 += KU) {
+            float4 v[KU][OPT];
 #pragma unroll
-        for (int k = 0; k < OPT; ++k) {
-            const int o = tid + kThreads * k;
-            if (o >= nout) continue;
-            const int rr = o / D4, hh = rr / G, r = rr % G, c4 = o % D4;
-            const float mx = s_max[rr], sc = s_scale[rr];
-            float4 a = acc[k];
-            a.x *= sc;
-            a.y *= sc;
-            a.z *= sc;
-            a.w *= sc;
-            for (uint32_t i = 0; i < np; ++i) {
-                const float* pa = reinterpret_cast<const float*>(stage + i * piece_bytes);
-                const float2* ml = reinterpret_cast<const float2*>(stage + i * piece_bytes + acc_bytes);
+            for (int u = 0; u < KU; ++u) {
 #pragma unroll
-                for (int jj = 0; jj < J; ++jj) {
-                    const float mk = ml[(hh * J + jj) * G + r].x;
-                    if (mk == -INFINITY) continue;
-                    const float w = exp2f(mk - mx);
-                    const float4 v = reinterpret_cast<const float4*>(pa + ((hh * J + jj) * G + r) * D)[c4];
-                    a.x += w * v.x;
-                    a.y += w * v.y;
-                    a.z += w * v.z;
-                    a.w += w * v.w;
+                for (int i = 0; i < OPT; ++i) {
+                    const int o = tid + kThreads * i;
+                    const int kk = kk0 + u;
+                    v[u][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (o < nout && kk < nk) {
+                        const int rr = o / D4;
+                        if (s_wm[kk * R + rr] != 0.f)
+                            v[u][i] = __ldcg(reinterpret_cast<const float4*>(
+                                                 rec_acc + (rec_of(k0 + kk, rr / G) * G + rr % G) * D) +
+                                             (o % D4));
+                    }
                 }
             }
-            acc[k] = a;
+#pragma unroll
+            for (int u = 0; u < KU; ++u) {
+#pragma unroll
+                for (int i = 0; i < OPT; ++i) {
+                    const int o = tid + kThreads * i;
+                    const int kk = kk0 + u;
+                    if (o < nout && kk < nk) {
+                        const float w = s_wm[kk * R + o / D4];
+                        acc[i].x += w * v[u][i].x;
+                        acc[i].y += w * v[u][i].y;
+                        acc[i].z += w * v[u][i].z;
+                        acc[i].w += w * v[u][i].w;
+                    }
+                }
+            }
         }
-        named_barrier(1, kThreads);  // the next chunk overwrites the shared records
+        named_barrier(1, kThreads);  // the next chunk rewrites the shared arrays
     }
     const uint32_t seq = static_cast<uint32_t>(sg) / head_groups;
     const uint32_t kv0 = (static_cast<uint32_t>(sg) % head_groups) * HH;
 #pragma unroll
-    for (int k = 0; k < OPT; ++k) {
-        const int o = tid + kThreads * k;
+    for (int i = 0; i < OPT; ++i) {
+        const int o = tid + kThreads * i;
         if (o < nout) {
             const int rr = o / D4, hh = rr / G, r = rr % G;
-            const float inv = 1.f / s_sum[rr];
             __nv_bfloat16* ob =
                 out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kv0 + hh) * G + r) * D + (o % D4) * 4;
-            reinterpret_cast<uint32_t*>(ob)[0] = pack_bf16x2(acc[k].x * inv, acc[k].y * inv);
-            reinterpret_cast<uint32_t*>(ob)[1] = pack_bf16x2(acc[k].z * inv, acc[k].w * inv);
+            reinterpret_cast<uint32_t*>(ob)[0] = pack_bf16x2(acc[i].x, acc[i].y);
+            reinterpret_cast<uint32_t*>(ob)[1] = pack_bf16x2(acc[i].z, acc[i].w);
         }
     }
-    named_barrier(1, kThreads);  // s_stat is reused by the next merge
-    return true;
 }
 
 template <int D, int HH, int STAGES>
@@ -629,6 +728,9 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     const int lane = tid & 31;
     const int nseg = static_cast<int>(p.nseg);
     const uint32_t cap_tokens = p.pitch * 16u;
+    // scratch after the prefix, 16-byte aligned
+    float* scratch = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(prefix + nseg + 1) + 15) &
+                                              ~static_cast<uintptr_t>(15));
 
     // Launched as a programmatic dependent of the previous kernel on the
     // stream: everything above ran while it drained; wait for it (and its
@@ -665,16 +767,24 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     // The next decode on the stream may be scheduled from here on; it waits
     // (griddepcontrol.wait) for this whole grid before it touches memory.
     grid_launch_dependents();
-    const uint32_t x0 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x) * total / gridDim.x);
-    const uint32_t x1 = static_cast<uint32_t>(static_cast<uint64_t>(blockIdx.x + 1) * total / gridDim.x);
+    const uint32_t grid = gridDim.x;
+    StreamSplit split;
+    split.prefix = prefix;
+    split.nseg = nseg;
+    split.total = total;
+    split.grid = grid;
+    split.b = p.seg_cost;
+    split.cost = static_cast<uint64_t>(total) + static_cast<uint64_t>(p.seg_cost) * nseg;
+    const uint32_t x0 = split.begin(blockIdx.x);
+    const uint32_t x1 = split.begin(blockIdx.x + 1);
     if (x0 >= x1) return;
-    const int sg0 = find_segment(prefix, nseg, x0);
+    const PieceOrder order(prefix, nseg, x0, x1);
 
     const uint32_t full0 = smem_u32(bars);
     const uint32_t empty0 = smem_u32(bars + STAGES);
     __shared__ int s_dead;  // a consumer warp's pipeline wait gave up
-    __shared__ uint32_t s_merge_bits[kStreamMaxSegments / 32];  // segments this CTA merges
-    for (int i = tid; i < kStreamMaxSegments / 32; i += kFastThreads) s_merge_bits[i] = 0u;
+    __shared__ int s_last;  // this CTA completed the segment it just finished
+    __shared__ float s_stat[128];
     if (tid == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(full0 + 8 * s, 1);
@@ -686,71 +796,66 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     __syncthreads();
 
     if (warp == kFastComputeWarps) {
-        // Producer warp: lane 0 issues; all lanes keep a 32-entry window of
+        // Producer warp: lane 0 issues; all lanes keep two 32-entry windows of
         // the current segment's block table so entries arrive 32 at a time.
         const uint64_t policy = l2_policy_evict_first();
-        if (lane == 0) prefetch_tensormap(&tmap);
-        int sg = sg0;
-        uint32_t seg_begin = prefix[sg], seg_end = prefix[sg + 1];
-        int seq = sg / p.head_groups, hg = sg % p.head_groups;
-        uint32_t units = (static_cast<uint32_t>(p.ctx[seq]) + 15u) / 16u;
-        const int32_t* row = p.tables + static_cast<size_t>(seq) * p.pitch;
-        // two 32-entry windows of the table row: the next one is loaded while
-        // the current one is streamed, so a refill never stalls the producer
-        int win = -1;
-        int32_t entry = 0, entry_next = 0;
-        for (uint32_t x = x0; x < x1; ++x) {
-            if (x >= seg_end) {
-                do {
-                    ++sg;
-                    seg_begin = prefix[sg];
-                    seg_end = prefix[sg + 1];
-                } while (x >= seg_end);
-                seq = sg / p.head_groups;
-                hg = sg % p.head_groups;
-                units = (static_cast<uint32_t>(p.ctx[seq]) + 15u) / 16u;
-                row = p.tables + static_cast<size_t>(seq) * p.pitch;
-                win = -1;
-            }
-            const uint32_t it = x - x0;
-            const uint32_t slot = it % STAGES;
-            const int blk0 = static_cast<int>((x - seg_begin) * J);
-            if (win < 0 || blk0 < win || blk0 + J > win + 64) {
-                win = blk0;
-                entry = (static_cast<uint32_t>(win + lane) < units) ? row[win + lane] : 0;
-                entry_next = (static_cast<uint32_t>(win + 32 + lane) < units) ? row[win + 32 + lane] : 0;
-            } else if (blk0 + J > win + 32) {
-                win += 32;  // J divides 32, so blk0 == win here
-                entry = entry_next;
-                entry_next = (static_cast<uint32_t>(win + 32 + lane) < units) ? row[win + 32 + lane] : 0;
-            }
-            int32_t ids[J];
+        uint32_t it = 0;
+        bool ok_all = true;
+        for (int pi = 0; pi < order.count && ok_all; ++pi) {
+            int sg;
+            uint32_t pb, pe;
+            bool whole;
+            order.at(prefix, pi, sg, pb, pe, whole);
+            if (pb >= pe) continue;
+            const uint32_t seg_begin = static_cast<uint32_t>(prefix[sg]);
+            const int seq = sg / p.head_groups, hg = sg % p.head_groups;
+            const uint32_t units = (static_cast<uint32_t>(p.ctx[seq]) + 15u) / 16u;
+            const int32_t* row = p.tables + static_cast<size_t>(seq) * p.pitch;
+            int win = -1;
+            int32_t entry = 0, entry_next = 0;
+            for (uint32_t x = pb; x < pe; ++x, ++it) {
+                const uint32_t slot = it % STAGES;
+                const int blk0 = static_cast<int>((x - seg_begin) * J);
+                if (win < 0 || blk0 < win || blk0 + J > win + 64) {
+                    win = blk0;
+                    entry = (static_cast<uint32_t>(win + lane) < units) ? row[win + lane] : 0;
+                    entry_next = (static_cast<uint32_t>(win + 32 + lane) < units) ? row[win + 32 + lane] : 0;
+                } else if (blk0 + J > win + 32) {
+                    win += 32;  // J divides 32, so blk0 == win here
+                    entry = entry_next;
+                    entry_next = (static_cast<uint32_t>(win + 32 + lane) < units) ? row[win + 32 + lane] : 0;
+                }
+                int32_t ids[J];
 #pragma unroll
-            for (int j = 0; j < J; ++j) ids[j] = __shfl_sync(0xffffffffu, entry, blk0 - win + j);
-            int ok = 1;
-            if (lane == 0) {
-                if (it >= STAGES && !mbar_wait_bounded(empty0 + 8 * slot, ((it / STAGES) - 1) & 1u)) {
-                    record_error(p.err, kErrWaitTimeout);
-                    ok = 0;
-                } else {
-                    const uint32_t nb = min(static_cast<uint32_t>(J), units - static_cast<uint32_t>(blk0));
-                    mbar_arrive_expect_tx(full0 + 8 * slot, nb * S::kBlock);
-                    const uint32_t dst = smem_u32(smem + slot * S::kStage);
+                for (int j = 0; j < J; ++j) ids[j] = __shfl_sync(0xffffffffu, entry, blk0 - win + j);
+                int ok = 1;
+                if (lane == 0) {
+                    if (it >= STAGES && !mbar_wait_bounded(empty0 + 8 * slot, ((it / STAGES) - 1) & 1u)) {
+                        record_error(p.err, kErrWaitTimeout);
+                        ok = 0;
+                    } else {
+                        const uint32_t nb = min(static_cast<uint32_t>(J), units - static_cast<uint32_t>(blk0));
+                        mbar_arrive_expect_tx(full0 + 8 * slot, nb * S::kBlock);
+                        const uint32_t dst = smem_u32(smem + slot * S::kStage);
 #pragma unroll
-                    for (int j = 0; j < J; ++j) {
-                        if (static_cast<uint32_t>(j) < nb) {
-                            int32_t id = ids[j];
-                            if (static_cast<uint32_t>(id) >= p.num_blocks) {
-                                record_error(p.err, kErrBadBlockId);
-                                id = 0;
+                        for (int j = 0; j < J; ++j) {
+                            if (static_cast<uint32_t>(j) < nb) {
+                                int32_t id = ids[j];
+                                if (static_cast<uint32_t>(id) >= p.num_blocks) {
+                                    record_error(p.err, kErrBadBlockId);
+                                    id = 0;
+                                }
+                                const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
+                                tma_load_4d(dst + j * S::kBlock, &tmap, full0 + 8 * slot, 0, r, hg * HH, 0, policy);
                             }
-                            const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
-                            tma_load_4d(dst + j * S::kBlock, &tmap, full0 + 8 * slot, 0, r, hg * HH, 0, policy);
                         }
                     }
                 }
+                if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                    ok_all = false;
+                    break;
+                }
             }
-            if (!__shfl_sync(0xffffffffu, ok, 0)) break;
         }
         return;
     }
@@ -761,124 +866,205 @@ __global__ void __launch_bounds__(kFastThreads, 1)
     const int g = lane >> 2;
     const int c = lane & 3;
     const int G = static_cast<int>(p.group);
-    const uint32_t grid = gridDim.x;
-    __shared__ float s_stat[196];  // merge: running max, sum, rescale per row; a vote
-
-    int sg = sg0;
-    uint32_t seg_begin = prefix[sg], seg_end = prefix[sg + 1];
-    int seq = sg / p.head_groups, hg = sg % p.head_groups;
-    int ctx = p.ctx[seq];
-    uint32_t units = (static_cast<uint32_t>(ctx) + 15u) / 16u;
+    constexpr int kConsumers = kFastComputeWarps * 32;
+    const uint32_t state_floats = static_cast<uint32_t>(G * D + 2 * G);
 
     uint32_t qa[KS][4];
     WarpState<D> st;
     bool alive = true;
+    uint32_t it = 0;
 
-    // Writes this warp's partial (accumulator rows < G, max, sum) for the
-    // current segment piece as record (sg + blockIdx.x, hh, j) and counts the
-    // CTA's piece; the CTA whose piece completes the count marks the segment
-    // for merging after its stream. Reached by all consumer warps at the same
-    // stage (segment ends are CTA-uniform).
-    auto finish_piece = [&]() {
-        float a0 = st.l0 + __shfl_xor_sync(0xffffffffu, st.l0, 1);
-        a0 += __shfl_xor_sync(0xffffffffu, a0, 2);
-        float a1 = st.l1 + __shfl_xor_sync(0xffffffffu, st.l1, 1);
-        a1 += __shfl_xor_sync(0xffffffffu, a1, 2);
-        const size_t rec = ((static_cast<size_t>(sg) + blockIdx.x) * HH + hh) * J + j;
-        float* wo = p.rec_acc + rec * G * D;
-#pragma unroll
-        for (int n = 0; n < NT; ++n) {
-            const int col = n * 8 + c * 2;
-            if (g < G) *reinterpret_cast<float2*>(wo + g * D + col) = make_float2(st.o[n][0], st.o[n][1]);
-            if (g + 8 < G) *reinterpret_cast<float2*>(wo + (g + 8) * D + col) = make_float2(st.o[n][2], st.o[n][3]);
+    // the first piece's query fragments
+    int next_pi = 0;
+    int n_sg = 0;
+    uint32_t n_b = 0, n_e = 0;
+    bool n_whole = false;
+    auto find_next = [&](int from) {
+        for (int pi = from; pi < order.count; ++pi) {
+            order.at(prefix, pi, n_sg, n_b, n_e, n_whole);
+            if (n_b < n_e) return pi;
         }
-        if (c == 0) {
-            if (g < G) p.rec_ml[rec * G + g] = make_float2(st.m0, a0);
-            if (g + 8 < G) p.rec_ml[rec * G + g + 8] = make_float2(st.m1, a1);
-        }
-        // the records reach L2, for the generic and the async (bulk copy)
-        // proxies, before the arrival is counted
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        __threadfence();
-        named_barrier(1, kFastComputeWarps * 32);
-        if (tid == 0) {
-            uint32_t cf, cl;
-            pieces_of(seg_begin, seg_end, total, grid, cf, cl);
-            uint32_t expected = cl - cf + 1;
-            if (total < grid) {
-                expected = 0;
-                for (uint32_t cc = cf; cc <= cl; ++cc) expected += cta_is_empty(cc, total, grid) ? 0u : 1u;
-            }
-            // the merge itself waits until the CTA's stream is done, so the
-            // pipeline is never held up by it
-            if (expected <= 1 || arrive_last(p.seg_count + sg, p.epoch, expected)) {
-                __threadfence();  // the other pieces' records are read after this
-                s_merge_bits[sg >> 5] |= 1u << (sg & 31);
-            }
-        }
+        return order.count;
     };
+    next_pi = find_next(0);
+    if (next_pi < order.count)
+        load_query_fragments<D>(qa, p.q, n_sg / p.head_groups, p.hq, (n_sg % p.head_groups) * HH + hh, G, lane);
 
-    load_query_fragments<D>(qa, p.q, seq, p.hq, hg * HH + hh, G, lane);
-    st.reset();
-    for (uint32_t x = x0; x < x1; ++x) {
-        if (x >= seg_end) {
-            finish_piece();
-            do {
-                ++sg;
-                seg_begin = prefix[sg];
-                seg_end = prefix[sg + 1];
-            } while (x >= seg_end);
-            seq = sg / p.head_groups;
-            hg = sg % p.head_groups;
-            ctx = p.ctx[seq];
-            units = (static_cast<uint32_t>(ctx) + 15u) / 16u;
-            load_query_fragments<D>(qa, p.q, seq, p.hq, hg * HH + hh, G, lane);
-            st.reset();
+    while (next_pi < order.count) {
+        const int sg = n_sg;
+        const uint32_t pb = n_b, pe = n_e;
+        const bool whole = n_whole;
+        const uint32_t seg_begin = static_cast<uint32_t>(prefix[sg]);
+        const int seq = sg / p.head_groups, hg = sg % p.head_groups;
+        const int ctx = p.ctx[seq];
+        const uint32_t units = (static_cast<uint32_t>(ctx) + 15u) / 16u;
+        st.reset();
+        for (uint32_t x = pb; x < pe; ++x, ++it) {
+            const uint32_t slot = it % STAGES;
+            if (alive && !mbar_wait_bounded(full0 + 8 * slot, (it / STAGES) & 1u)) {
+                // the warp stops computing but keeps meeting the CTA's
+                // barriers; the host sees the error bit and this CTA writes
+                // no output and no record
+                record_error(p.err, kErrWaitTimeout);
+                alive = false;
+                s_dead = 1;
+            }
+            const uint32_t blk = (x - seg_begin) * J + j;
+            if (alive && blk < units) {
+                const int valid = min(16, ctx - static_cast<int>(blk) * 16);
+                const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
+                attend_block<D, HH>(st, qa, kb, hh, valid, p.scale_log2, lane);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(empty0 + 8 * slot);
         }
-        const uint32_t it = x - x0;
-        const uint32_t slot = it % STAGES;
-        if (alive && !mbar_wait_bounded(full0 + 8 * slot, (it / STAGES) & 1u)) {
-            // the warp stops computing but keeps meeting the CTA's barriers;
-            // the host sees the error bit, and no segment this CTA completes
-            // is merged
-            record_error(p.err, kErrWaitTimeout);
-            alive = false;
-            s_dead = 1;
+        // The next piece's query rows: after a whole segment they start
+        // loading now and arrive during the epilogue; after a shared piece
+        // they load once its record is out (and any merge is done), so that
+        // no query registers are live across the merge.
+        next_pi = find_next(next_pi + 1);
+        auto load_next_query = [&]() {
+            if (next_pi < order.count)
+                load_query_fragments<D>(qa, p.q, n_sg / p.head_groups, p.hq, (n_sg % p.head_groups) * HH + hh, G,
+                                        lane);
+        };
+
+        // Epilogue. Row sums over the lane quad first.
+        float l0 = st.l0 + __shfl_xor_sync(0xffffffffu, st.l0, 1);
+        l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+        float l1 = st.l1 + __shfl_xor_sync(0xffffffffu, st.l1, 1);
+        l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+        float m0 = st.m0, m1 = st.m1;
+        auto& o = st.o;
+        // Combine the J warp columns of each head into column 0: a tree of
+        // rounds; in each, columns [half, 2*half) hand their state over.
+#pragma unroll
+        for (int half = J / 2; half >= 1; half >>= 1) {
+            if (j >= half && j < 2 * half) {
+                float* w = scratch + static_cast<uint32_t>((j - half) * HH + hh) * state_floats;
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    const int col = n * 8 + c * 2;
+                    if (g < G) *reinterpret_cast<float2*>(w + g * D + col) = make_float2(o[n][0], o[n][1]);
+                    if (g + 8 < G) *reinterpret_cast<float2*>(w + (g + 8) * D + col) = make_float2(o[n][2], o[n][3]);
+                }
+                if (c == 0) {
+                    if (g < G) {
+                        w[G * D + g] = m0;
+                        w[G * D + G + g] = l0;
+                    }
+                    if (g + 8 < G) {
+                        w[G * D + g + 8] = m1;
+                        w[G * D + G + g + 8] = l1;
+                    }
+                }
+            }
+            named_barrier(1, kConsumers);
+            if (j < half) {
+                const float* w = scratch + static_cast<uint32_t>(j * HH + hh) * state_floats;
+                const float mj0 = g < G ? w[G * D + g] : -INFINITY;
+                const float mj1 = g + 8 < G ? w[G * D + g + 8] : -INFINITY;
+                const float lj0 = g < G ? w[G * D + G + g] : 0.f;
+                const float lj1 = g + 8 < G ? w[G * D + G + g + 8] : 0.f;
+                const float M0 = fmaxf(m0, mj0), M1 = fmaxf(m1, mj1);
+                const float a0 = (m0 == -INFINITY) ? 0.f : exp2f(m0 - M0);
+                const float a1 = (m1 == -INFINITY) ? 0.f : exp2f(m1 - M1);
+                const float e0 = (mj0 == -INFINITY) ? 0.f : exp2f(mj0 - M0);
+                const float e1 = (mj1 == -INFINITY) ? 0.f : exp2f(mj1 - M1);
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    // keep the loads next to their use (a full hoist would
+                    // hold 2 * NT more registers than the kernel has)
+                    asm volatile("" ::: "memory");
+                    const int col = n * 8 + c * 2;
+                    const float2 lo = g < G ? *reinterpret_cast<const float2*>(w + g * D + col) : make_float2(0.f, 0.f);
+                    const float2 hi =
+                        g + 8 < G ? *reinterpret_cast<const float2*>(w + (g + 8) * D + col) : make_float2(0.f, 0.f);
+                    o[n][0] = o[n][0] * a0 + lo.x * e0;
+                    o[n][1] = o[n][1] * a0 + lo.y * e0;
+                    o[n][2] = o[n][2] * a1 + hi.x * e1;
+                    o[n][3] = o[n][3] * a1 + hi.y * e1;
+                }
+                l0 = l0 * a0 + lj0 * e0;
+                l1 = l1 * a1 + lj1 * e1;
+                m0 = M0;
+                m1 = M1;
+            }
+            named_barrier(1, kConsumers);
         }
-        const uint32_t blk = (x - seg_begin) * J + j;
-        if (alive && blk < units) {
-            const int valid = min(16, ctx - static_cast<int>(blk) * 16);
-            const uint32_t kb = smem_u32(smem + slot * S::kStage + j * S::kBlock);
-            attend_block<D, HH>(st, qa, kb, hh, valid, p.scale_log2, lane);
+        const bool dead = s_dead != 0;
+        if (whole) {
+            // the segment lies wholly in this CTA: write its output now
+            if (j == 0 && !dead) {
+                const float inv0 = 1.f / l0, inv1 = 1.f / l1;
+                __nv_bfloat16* ob =
+                    p.out + (static_cast<size_t>(seq) * p.hq + static_cast<size_t>(hg * HH + hh) * G) * D;
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+                    const int col = n * 8 + c * 2;
+                    if (g < G)
+                        *reinterpret_cast<uint32_t*>(ob + g * D + col) = pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
+                    if (g + 8 < G)
+                        *reinterpret_cast<uint32_t*>(ob + (g + 8) * D + col) =
+                            pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
+                }
+            }
+            load_next_query();
+            continue;
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * slot);
-    }
-    finish_piece();
-    named_barrier(1, kFastComputeWarps * 32);
-    if (s_dead != 0) return;  // records of this CTA are not to be trusted: merge nothing
-    // Merge the segments whose last piece this CTA completed (sg0 .. sg),
-    // through the pipeline's shared memory (the stream is done with it).
-    const int nout = HH * G * (D / 4);
-    __shared__ __align__(8) uint64_t s_merge_bar;
-    const uint32_t mbar = smem_u32(&s_merge_bar);
-    if (tid == 0) {
-        mbar_init(mbar, 1);
-        mbar_fence_init();
-    }
-    named_barrier(1, kFastComputeWarps * 32);
-    uint32_t phase = 0;
-    for (int ms = sg0; ms <= sg; ++ms) {
-        if ((s_merge_bits[ms >> 5] & (1u << (ms & 31))) == 0) continue;
+        // a shared piece: one record per head, then count the piece
+        if (j == 0 && !dead) {
+            const size_t rec = (static_cast<size_t>(sg) + blockIdx.x) * HH + hh;
+            float* wo = p.rec_acc + rec * G * D;
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const int col = n * 8 + c * 2;
+                if (g < G) *reinterpret_cast<float2*>(wo + g * D + col) = make_float2(o[n][0], o[n][1]);
+                if (g + 8 < G) *reinterpret_cast<float2*>(wo + (g + 8) * D + col) = make_float2(o[n][2], o[n][3]);
+            }
+            if (c == 0) {
+                if (g < G) p.rec_ml[rec * G + g] = make_float2(m0, l0);
+                if (g + 8 < G) p.rec_ml[rec * G + g + 8] = make_float2(m1, l1);
+            }
+            __threadfence();  // the record reaches L2 before the arrival is counted
+        }
+        named_barrier(1, kConsumers);
         uint32_t cf, cl;
-        pieces_of(static_cast<uint32_t>(prefix[ms]), static_cast<uint32_t>(prefix[ms + 1]), total, grid, cf, cl);
+        split.pieces(sg, cf, cl);
+        if (tid == 0) {
+            uint32_t expected = cl - cf + 1;
+            if (split.may_have_empty()) {
+                expected = 0;
+                for (uint32_t cc = cf; cc <= cl; ++cc) expected += split.empty(cc) ? 0u : 1u;
+            }
+            const bool last = !dead && arrive_last(p.seg_count + sg, p.epoch, expected);
+            if (last) __threadfence();  // the other pieces' records are read after this
+            s_last = last ? 1 : 0;
+        }
+        named_barrier(1, kConsumers);
+        if (s_last) {
+            // this piece completed the segment: merge it now (the producer
+            // warp keeps streaming meanwhile); the scratch holds the weights
+            const int R = HH * G;
+            const int nout = R * (D / 4);
+            const int chunk = min(32, static_cast<int>(4u * state_floats) / (2 * R));
+            float* s_wm = scratch;
+            float* s_wl = scratch + chunk * R;
 #define QVP_MERGE(OPT)                                                                                              \
-    merge_segment<D, HH, J, OPT>(p.rec_acc, p.rec_ml, p.out, p.group, p.head_groups, p.hq, ms, cf, cl, total, grid, \
-                                 smem, STAGES * S::kStage, mbar, phase, s_stat, tid, p.err)
-        const bool merged = nout <= 256 ? QVP_MERGE(1) : nout <= 512 ? QVP_MERGE(2) : nout <= 1024 ? QVP_MERGE(4)
-                                                                                          : QVP_MERGE(8);
+    merge_records<D, HH, OPT>(p.rec_acc, p.rec_ml, p.out, p.group, p.head_groups, p.hq, sg, cf, cl, split, s_wm, \
+                              s_wl, chunk, s_stat, tid)
+            if (nout <= 256)
+                QVP_MERGE(1);
+            else if (nout <= 512)
+                QVP_MERGE(2);
+            else if (nout <= 1024)
+                QVP_MERGE(4);
+            else
+                QVP_MERGE(8);
 #undef QVP_MERGE
-        if (!merged) break;
+            named_barrier(1, kConsumers);  // the scratch is the next piece's again
+        }
+        load_next_query();
     }
 }
 
@@ -1151,18 +1337,16 @@ int launch_fast(const qvp_decode_args& a, const DecodePlan& plan, const FastPara
 template <int D, int HH, int STAGES>
 int launch_stream_t(const qvp_decode_args& a, const DecodePlan& plan, const StreamParams& sp, cudaStream_t st) {
     using S = FastShape<D, HH, STAGES>;
-    constexpr int J = S::J;
-    constexpr uint32_t kMaxSmem = S::kSmem + (kStreamMaxSegments + 1) * 4;
-    static_assert(kMaxSmem <= 232448, "stream decode exceeds the 227 KB shared-memory limit");
+    static_assert(S::kSmem == stream_pipeline_smem(D), "stream decode pipeline size");
     static std::atomic<std::uint64_t> attr_done{0};
     auto kern = paged_decode_stream<D, HH, STAGES>;
-    int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern), static_cast<int>(kMaxSmem),
+    int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern), static_cast<int>(kMaxDynamicSmem),
                                  "cudaFuncSetAttribute(stream decode)");
     if (rc != QVP_OK) return rc;
     CUtensorMap map;
     rc = encode_pool_map(a.pool, a.num_blocks, a.shape, HH, &map);
     if (rc != QVP_OK) return rc;
-    const uint32_t smem = kMaxSmem;
+    const uint32_t smem = static_cast<uint32_t>(stream_smem_bytes(sp.nseg, sp.group, D));
     {
         // programmatic dependent of whatever precedes it on the stream (the
         // previous step's decode): the prologue overlaps that kernel's tail
@@ -1241,14 +1425,14 @@ int plan_decode(const qvp_decode_args& a, DecodePlan& plan) {
     if (plan.fast && a.split_tokens == 0) {
         const uint32_t z = sh.num_kv_heads / plan.heads_per_cta;
         const uint64_t nseg = static_cast<uint64_t>(a.batch) * z;
-        if (nseg <= static_cast<uint64_t>(kStreamMaxSegments)) {
+        if (nseg <= static_cast<uint64_t>(kStreamMaxSegments) &&
+            stream_smem_bytes(static_cast<uint32_t>(nseg), plan.group, sh.head_dim) <= kMaxDynamicSmem) {
             // Persistent stream-K: one CTA per SM over the whole stage stream.
             plan.stream = true;
             plan.nseg = static_cast<uint32_t>(nseg);
             const int sms = device_sm_count();
             plan.grid_ctas = sms > 0 ? static_cast<uint32_t>(sms) : 148u;
-            const uint32_t J = 8u / plan.heads_per_cta;
-            const size_t records = (static_cast<size_t>(plan.nseg) + plan.grid_ctas) * plan.heads_per_cta * J;
+            const size_t records = (static_cast<size_t>(plan.nseg) + plan.grid_ctas) * plan.heads_per_cta;
             plan.records = records;
             plan.split_tokens = 0;
             plan.max_splits = 1;
@@ -1344,6 +1528,10 @@ int qvp::run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream
         sp.seg_count = reinterpret_cast<unsigned long long*>(ws + acc_bytes + ml_bytes);
         sp.out = static_cast<__nv_bfloat16*>(a.out);
         sp.epoch = next_epoch();
+        // fixed cost of a segment in stage-equivalents: its epilogue combines
+        // J warp columns (log2 J rounds) and a shared piece adds a record
+        // and, for one CTA, the merge; measured on cfg2-shaped batches
+        sp.seg_cost = kSegmentCostStages[plan.heads_per_cta == 4 ? 2 : plan.heads_per_cta == 2 ? 1 : 0];
         sp.err = a.error_word;
         sp.pitch = a.max_blocks_per_seq;
         sp.num_blocks = a.num_blocks;

@@ -53,6 +53,19 @@ std::size_t HostSwapBackend::capacity_slots() const noexcept { return max_slots_
 namespace {
 
 constexpr std::size_t kMaxStagingBytes = std::size_t(256) << 20;
+// Largest single PCIe copy: a small copy the engine stream enqueues meanwhile
+// (a decode's table upload) may queue on the same copy engine behind one.
+// Smaller pieces mean more calls per flush, and past about a thousand queued
+// copies the host call itself blocks (8 MiB pieces held a 15 GB swap-out's
+// flush on the host for 130 ms).
+constexpr std::size_t kMaxCopyBytes = std::size_t(64) << 20;
+
+// cudaMemcpyAsync of `bytes` in pieces of at most kMaxCopyBytes.
+void copy_in_pieces(void* dst, const void* src, std::size_t bytes, cudaMemcpyKind kind, cudaStream_t st) {
+    for (std::size_t off = 0; off < bytes; off += kMaxCopyBytes)
+        cudaMemcpyAsync(static_cast<std::byte*>(dst) + off, static_cast<const std::byte*>(src) + off,
+                        std::min(kMaxCopyBytes, bytes - off), kind, st);
+}
 
 using host_impl::OnDevice;
 
@@ -234,15 +247,15 @@ void DeviceSwapBackend::flush_moves(std::vector<Move>& moves, bool stores, std::
                                   copy_) != QVP_OK)
                 note(std::string("swap-out gather: ") + qvp_last_error());
             for_each_run(idx.data() + base, n, [&](std::size_t first, std::size_t count) {
-                cudaMemcpyAsync(slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
-                                staging_ + first * slot_bytes_, count * slot_bytes_, cudaMemcpyDeviceToHost, copy_);
+                copy_in_pieces(slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
+                               staging_ + first * slot_bytes_, count * slot_bytes_, cudaMemcpyDeviceToHost, copy_);
             });
             bytes_out_ += n * slot_bytes_;
         } else {
             for_each_run(idx.data() + base, n, [&](std::size_t first, std::size_t count) {
-                cudaMemcpyAsync(staging_ + first * slot_bytes_,
-                                slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
-                                count * slot_bytes_, cudaMemcpyHostToDevice, copy_);
+                copy_in_pieces(staging_ + first * slot_bytes_,
+                               slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
+                               count * slot_bytes_, cudaMemcpyHostToDevice, copy_);
             });
             if (qvp_scatter_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(),
                                    slot_bytes_, ids_dev + base, static_cast<std::uint32_t>(n), staging_, nullptr,
