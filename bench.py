@@ -51,7 +51,7 @@ FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the dominant
 # kernel (paged_decode_stream) on the default workload, from the ncu capture
 # summarised in profiles/paged_decode_stream_cfg2.md.
-NCU_TRAFFIC_BYTES = {"cfg2-qwen2vl-7b-decode": 603_610_368 + 5_478_912}
+NCU_TRAFFIC_BYTES = {"cfg2-qwen2vl-7b-decode": 603_664_128 + 4_811_776}
 
 
 def measured_peak():
