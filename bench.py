@@ -150,6 +150,18 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _device_bytes(ptr, nbytes, dev):
+    """A uint8 torch view of `nbytes` of device memory at `ptr` (memory that
+    libqvp owns)."""
+    import torch
+
+    class _Raw:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+
+    return torch.as_tensor(_Raw(), device=dev)
+
+
 def run_ours(args):
     import ctypes
 
@@ -205,7 +217,18 @@ def run_ours(args):
                    else "paged_decode_generic + combine_partitions")
 
     comm = None
-    if sharded and not args.no_gather:
+    peer = None
+    if sharded and not args.no_gather and args.exchange == "peer":
+        # every GPU of a head group stores its output rows into every other
+        # GPU's buffer over NVLink (libqvp's peer group); handles travel over
+        # torch.distributed
+        import torch.distributed as dist
+        peer = qvp.PeerGroup(head_part, hp, out.numel() * out.element_size())
+        handles = [None] * world
+        dist.all_gather_object(handles, peer.handle)
+        peer.open(handles[batch_part * hp:(batch_part + 1) * hp])
+        launches_per_step += 1  # peer_signal_wait
+    elif sharded and not args.no_gather:
         # one NCCL communicator per head group (the hp GPUs that share a batch),
         # made by libqvp; the unique id travels over torch.distributed
         import torch.distributed as dist
@@ -219,13 +242,27 @@ def run_ours(args):
 
     gathered = []
     sa = None
-    if comm is not None:
+    if peer is not None:
+        sa = shard_args(a, 0, 0)
+    elif comm is not None:
         sa = shard_args(a, out.data_ptr(), 0)
         gathered.append(torch.empty(qvp.shard_gather_bytes(sa), dtype=torch.uint8, device=dev))
         sa.gathered = gathered[0].data_ptr()
 
-    def run_step(decode_args, shard_decode_args, st):
-        if shard_decode_args is not None:
+    peer_step = [0]
+
+    def run_step(decode_args, shard_decode_args, st, copy_to=None):
+        if peer is not None:
+            rc = peer.decode(shard_decode_args, peer_step[0], err.data_ptr(), st)
+            what = "qvp_shard_decode_peer"
+            if rc == 0 and copy_to is not None:
+                # the step's output (every head) sits in the group buffer of
+                # this step's parity; hand it to the download buffer
+                nbytes = copy_to.numel() * copy_to.element_size()
+                copy_to.view(-1).view(torch.uint8).copy_(
+                    _device_bytes(peer.output(peer_step[0]), nbytes, dev), non_blocking=True)
+            peer_step[0] += 1
+        elif shard_decode_args is not None:
             rc = qvp.lib.qvp_shard_decode(ctypes.byref(shard_decode_args), st)
             what = "qvp_shard_decode"
         else:
@@ -286,6 +323,10 @@ def run_ours(args):
     sampler.stop()
     if int(err.item()) != 0:
         raise RuntimeError(f"decode kernel reported device error bits {int(err.item())}")
+    if peer is not None:
+        # the device-resident run's output: every head of the last step
+        out.view(-1).view(torch.uint8).copy_(_device_bytes(peer.output(peer_step[0] - 1), out.numel() * 2, dev))
+        torch.cuda.synchronize()
 
     ms_step = total_ms / args.steps
     alg = w.algorithmic_bytes()
@@ -327,7 +368,9 @@ def run_ours(args):
         ab.query = dev_in[b].data_ptr() + off_q
         ab.out = dev_out[b].data_ptr()
         args2.append(ab)
-        if comm is not None:
+        if peer is not None:
+            sargs2.append(shard_args(ab, 0, 0))
+        elif comm is not None:
             gathered.append(torch.empty_like(gathered[0]))
             sargs2.append(shard_args(ab, dev_out[b].data_ptr(), gathered[-1].data_ptr()))
         else:
@@ -346,7 +389,7 @@ def run_ours(args):
             ev_up[b].record(up_s)
             stream.wait_event(ev_up[b])
             stream.wait_event(ev_down[b])  # step i-2's outputs have left buffer b
-            run_step(args2[b], sargs2[b], sh)
+            run_step(args2[b], sargs2[b], sh, copy_to=dev_out[b] if peer is not None else None)
             ev_dec[b].record(stream)
             down_s.wait_event(ev_dec[b])
             with torch.cuda.stream(down_s):
@@ -381,15 +424,23 @@ def run_ours(args):
     if comm is not None:
         torch.cuda.synchronize()
         qvp.nccl_comm_destroy(comm)
+    if peer is not None:
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()  # no peer may still store into this GPU's buffers
+        peer.close()
 
     if rank == 0:
         traffic = NCU_TRAFFIC_BYTES.get(w.name)
         global_batch = w.batch * dp
         if sharded:
+            exch = ("; per step: decode storing every head's rows into every GPU of the head group over NVLink "
+                    "+ a flag exchange (libqvp peer group), inside the timed region" if peer is not None else
+                    "; per step: decode + NCCL all-gather (libqvp, in place) + reassemble kernel to [B, Hq, D] "
+                    "inside the timed region")
             parallelism = (f"kv-head shards x{hp} (each GPU {w.num_kv_heads} kv / {w.num_query_heads} q heads) "
-                           f"x sequence groups x{dp}" +
-                           ("" if args.no_gather else "; per step: decode + NCCL all-gather (libqvp, in place) "
-                                                      "+ reassemble kernel to [B, Hq, D] inside the timed region"))
+                           f"x sequence groups x{dp}" + ("" if args.no_gather else exch))
         elif world > 1:
             parallelism = f"sequence groups x{dp} (one batch per GPU, no collective)"
         else:
@@ -443,7 +494,8 @@ def run_ours(args):
                 "ms_per_step": round(e2e_ms, 5),
                 "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h),
-                "path": ("C ABI qvp_shard_decode" if comm is not None else "C ABI qvp_decode") +
+                "path": ("C ABI qvp_shard_decode_peer" if peer is not None else
+                         "C ABI qvp_shard_decode" if comm is not None else "C ABI qvp_decode") +
                         "; per step one H2D of tables+ctx+q from pinned memory and one D2H of "
                         "out, on two copy streams double-buffered against the decode",
             },
@@ -779,6 +831,8 @@ def main():
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     p.add_argument("--no-gather", action="store_true", help="kv-head shards: skip the output all-gather")
+    p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                   help="kv-head shards: outputs to every GPU by NVLink peer stores (peer) or NCCL all-gather")
     p.add_argument("--emulate-shards", type=int, choices=[0, 2, 4, 8], default=0,
                    help="one GPU: run the workload one GPU of an H-way kv-head split holds (profiling)")
     p.add_argument("--shard", choices=["hybrid", "heads"], default="hybrid",

@@ -316,6 +316,42 @@ QVP_API int qvp_shard_reassemble(const void* gathered, void* out, uint32_t num_s
                          uint32_t batch, uint32_t heads_per_shard, uint32_t head_dim,
                          uint32_t bytes_per_element, qvp_stream_t stream);
 
+/* ---------------------------------------------------------------------------
+ * Output exchange over NVLink peer memory (the fused form of the shard
+ * all-gather): each GPU's decode kernel stores its heads' output rows
+ * straight into the output buffer of every GPU of the group, then a one-warp
+ * kernel raises this GPU's flag on every peer and waits (bounded, about one
+ * second, error bit 2 on timeout) for every peer's flag, all on the caller's
+ * stream. No NCCL and no reassembly pass.
+ *
+ * Set-up, once per process: qvp_peer_group_create allocates this GPU's two
+ * output buffers (steps alternate between them) and flags, and writes an
+ * opaque QVP_PEER_HANDLE_BYTES handle (a CUDA IPC handle); the caller gathers
+ * every rank's handle by its own transport and hands all of them, in rank
+ * order, to qvp_peer_group_open. Every GPU of the group must be able to reach
+ * the others' memory (NVLink / NVSwitch).
+ *
+ * qvp_shard_decode_peer(step) writes step's output into buffer step % 2 of
+ * every GPU; qvp_peer_group_output(group, step) is this GPU's copy, valid on
+ * the stream after the call. Steps must be issued in order 0, 1, 2, ... on
+ * every rank, and work reading the output of step k must be enqueued on the
+ * same stream before the decode of step k + 1 (peers overwrite that buffer
+ * in step k + 2). Needs the stream-K plan (bf16, head_dim 64/128, 16-token
+ * blocks). No counterpart in the reference.
+ * ------------------------------------------------------------------------- */
+#define QVP_PEER_HANDLE_BYTES 64
+typedef struct qvp_peer_group qvp_peer_group;
+
+QVP_API int qvp_peer_group_create(int rank, int nranks, size_t out_bytes, void* handle,
+                          qvp_peer_group** group);
+QVP_API int qvp_peer_group_open(qvp_peer_group* group, const void* handles);
+QVP_API int qvp_peer_group_destroy(qvp_peer_group* group);
+QVP_API void* qvp_peer_group_output(const qvp_peer_group* group, uint64_t step);
+/* args->nccl_comm and args->gathered are ignored; args->out is ignored (the
+ * output goes to the group's buffers). */
+QVP_API int qvp_shard_decode_peer(const qvp_shard_decode_args* args, qvp_peer_group* group,
+                          uint64_t step, int32_t* error_word, qvp_stream_t stream);
+
 /* NCCL communicator helpers for callers that have no NCCL binding of their
  * own (FFI callers): the unique id (QVP_NCCL_ID_BYTES opaque bytes) is made
  * on one rank and handed to the others by the caller's own transport. The

@@ -415,7 +415,7 @@ struct StreamParams {
     float* rec_acc;       // [records][G][D], records = (nseg + grid) * HH
     float2* rec_ml;       // [records][G]
     unsigned long long* seg_count;  // [nseg] arrival counters (epoch << 32 | pieces)
-    __nv_bfloat16* out;   // [batch][hq][D]
+    OutTargets out;
     int32_t* err;
     uint32_t pitch;
     uint32_t num_blocks;
@@ -596,8 +596,8 @@ struct PieceOrder {
 // order of summation depends on neither the merging CTA nor timing.
 template <int D, int HH, int OPT>
 __device__ __noinline__ void merge_records(const float* __restrict__ rec_acc, const float2* __restrict__ rec_ml,
-                                              __nv_bfloat16* __restrict__ out, uint32_t group, uint32_t head_groups,
-                                              uint32_t hq, int sg, uint32_t cf, uint32_t cl, StreamSplit split,
+                                              const OutTargets out, uint32_t group, uint32_t head_groups,
+                                              int sg, uint32_t cf, uint32_t cl, StreamSplit split,
                                               float* s_wm, float* s_wl, int chunk, float* s_stat, int tid) {
     constexpr int D4 = D / 4;
     constexpr int kThreads = kFastComputeWarps * 32;
@@ -701,10 +701,12 @@ __device__ __noinline__ void merge_records(const float* __restrict__ rec_acc, co
         const int o = tid + kThreads * i;
         if (o < nout) {
             const int rr = o / D4, hh = rr / G, r = rr % G;
-            __nv_bfloat16* ob =
-                out + (static_cast<size_t>(seq) * hq + static_cast<size_t>(kv0 + hh) * G + r) * D + (o % D4) * 4;
-            reinterpret_cast<uint32_t*>(ob)[0] = pack_bf16x2(acc[i].x, acc[i].y);
-            reinterpret_cast<uint32_t*>(ob)[1] = pack_bf16x2(acc[i].z, acc[i].w);
+            const uint32_t lo = pack_bf16x2(acc[i].x, acc[i].y), hi = pack_bf16x2(acc[i].z, acc[i].w);
+            for (uint32_t t = 0; t < out.n; ++t) {
+                __nv_bfloat16* ob = out.row(t, seq, (kv0 + hh) * G + r, D) + (o % D4) * 4;
+                reinterpret_cast<uint32_t*>(ob)[0] = lo;
+                reinterpret_cast<uint32_t*>(ob)[1] = hi;
+            }
         }
     }
 }
@@ -997,16 +999,18 @@ __global__ void __launch_bounds__(kFastThreads, 1)
             // the segment lies wholly in this CTA: write its output now
             if (j == 0 && !dead) {
                 const float inv0 = 1.f / l0, inv1 = 1.f / l1;
-                __nv_bfloat16* ob =
-                    p.out + (static_cast<size_t>(seq) * p.hq + static_cast<size_t>(hg * HH + hh) * G) * D;
+                for (uint32_t t = 0; t < p.out.n; ++t) {
+                    __nv_bfloat16* ob = p.out.row(t, seq, (hg * HH + hh) * G, D);
 #pragma unroll
-                for (int n = 0; n < NT; ++n) {
-                    const int col = n * 8 + c * 2;
-                    if (g < G)
-                        *reinterpret_cast<uint32_t*>(ob + g * D + col) = pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
-                    if (g + 8 < G)
-                        *reinterpret_cast<uint32_t*>(ob + (g + 8) * D + col) =
-                            pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
+                    for (int n = 0; n < NT; ++n) {
+                        const int col = n * 8 + c * 2;
+                        if (g < G)
+                            *reinterpret_cast<uint32_t*>(ob + g * D + col) =
+                                pack_bf16x2(o[n][0] * inv0, o[n][1] * inv0);
+                        if (g + 8 < G)
+                            *reinterpret_cast<uint32_t*>(ob + (g + 8) * D + col) =
+                                pack_bf16x2(o[n][2] * inv1, o[n][3] * inv1);
+                    }
                 }
             }
             load_next_query();
@@ -1051,8 +1055,8 @@ __global__ void __launch_bounds__(kFastThreads, 1)
             float* s_wm = scratch;
             float* s_wl = scratch + chunk * R;
 #define QVP_MERGE(OPT)                                                                                              \
-    merge_records<D, HH, OPT>(p.rec_acc, p.rec_ml, p.out, p.group, p.head_groups, p.hq, sg, cf, cl, split, s_wm, \
-                              s_wl, chunk, s_stat, tid)
+    merge_records<D, HH, OPT>(p.rec_acc, p.rec_ml, p.out, p.group, p.head_groups, sg, cf, cl, split, s_wm, s_wl, \
+                              chunk, s_stat, tid)
             if (nout <= 256)
                 QVP_MERGE(1);
             else if (nout <= 512)
@@ -1499,7 +1503,9 @@ extern "C" int qvp_decode(const qvp_decode_args* args, qvp_stream_t stream) {
     return run_decode(*args, plan, reinterpret_cast<cudaStream_t>(stream));
 }
 
-int qvp::run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream_t st) {
+int qvp::run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream_t st, const OutTargets* targets) {
+    if (targets != nullptr && !plan.stream)
+        return fail(QVP_ERR_UNSUPPORTED, "writing outputs to several GPUs needs the stream-K plan");
     int rc = QVP_OK;
     if (plan.workspace_bytes > 0 && (a.workspace == nullptr || a.workspace_bytes < plan.workspace_bytes))
         return fail(QVP_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", plan.workspace_bytes,
@@ -1526,7 +1532,14 @@ int qvp::run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream
         sp.rec_acc = reinterpret_cast<float*>(ws);
         sp.rec_ml = reinterpret_cast<float2*>(ws + acc_bytes);
         sp.seg_count = reinterpret_cast<unsigned long long*>(ws + acc_bytes + ml_bytes);
-        sp.out = static_cast<__nv_bfloat16*>(a.out);
+        if (targets != nullptr) {
+            sp.out = *targets;
+        } else {
+            sp.out.ptr[0] = static_cast<__nv_bfloat16*>(a.out);
+            sp.out.n = 1;
+            sp.out.head0 = 0;
+            sp.out.row_heads = a.num_query_heads;
+        }
         sp.epoch = next_epoch();
         // fixed cost of a segment in stage-equivalents: its epilogue combines
         // J warp columns (log2 J rounds) and a shared piece adds a record

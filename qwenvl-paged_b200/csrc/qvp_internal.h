@@ -4,6 +4,7 @@
 
 #include "qvp.h"
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -44,9 +45,31 @@ struct DecodePlan {
 
 // Validates `a` and fills `plan`; returns a qvp_status.
 int plan_decode(const qvp_decode_args& a, DecodePlan& plan);
+// Where the stream decode kernel writes each output row: the same
+// [batch][row_heads][head_dim] slice, at head offset head0, in each of n
+// buffers (n > 1: this GPU's buffer and its peers' over NVLink, for kv-head
+// shards whose outputs every GPU needs). A plain decode has n = 1, head0 = 0,
+// row_heads = num_query_heads.
+constexpr int kMaxOutTargets = 8;
+struct OutTargets {
+    __nv_bfloat16* ptr[kMaxOutTargets];
+    uint32_t n;
+    uint32_t head0;
+    uint32_t row_heads;
+
+#ifdef __CUDACC__
+    // Row of query head h of sequence seq in buffer i.
+    __device__ __forceinline__ __nv_bfloat16* row(uint32_t i, uint32_t seq, uint32_t h, uint32_t D) const {
+        return ptr[i] + (static_cast<size_t>(seq) * row_heads + head0 + h) * D;
+    }
+#endif
+};
+
 // Launches the decode `plan` (from plan_decode on the same arguments, batch
-// > 0) after checking the caller's workspace against it.
-int run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream_t st);
+// > 0) after checking the caller's workspace against it. `targets` (stream
+// plans only) replaces args.out by several destination buffers.
+int run_decode(const qvp_decode_args& a, const DecodePlan& plan, cudaStream_t st,
+               const OutTargets* targets = nullptr);
 
 int device_sm_count();
 

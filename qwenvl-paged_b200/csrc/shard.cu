@@ -237,3 +237,182 @@ extern "C" int qvp_nccl_comm_destroy(void* comm) {
     if (rc != QVP_OK) return rc;
     return check_nccl(nccl().comm_destroy(static_cast<ncclComm_t>(comm)), "ncclCommDestroy");
 }
+
+// ---- output exchange over NVLink peer memory -------------------------------
+
+struct qvp_peer_group {
+    int rank = 0, nranks = 0, device = -1;
+    size_t out_bytes = 0;
+    size_t buf_stride = 0;  // out_bytes rounded up to 256
+    uint8_t* local = nullptr;  // [2 buffers][flags: 2 parities x kMaxOutTargets sources x u64]
+    uint8_t* peer[qvp::kMaxOutTargets] = {};
+    bool opened = false;
+};
+
+namespace qvp {
+namespace {
+
+constexpr uint64_t kPeerWaitLimitNs = 1000000000ull;
+
+size_t flag_offset(const qvp_peer_group& g, uint32_t parity, uint32_t src) {
+    return 2 * g.buf_stride + (static_cast<size_t>(parity) * kMaxOutTargets + src) * sizeof(unsigned long long);
+}
+
+struct PeerSignal {
+    unsigned long long* remote[kMaxOutTargets];       // peer q's flag for (parity, this rank)
+    const unsigned long long* local[kMaxOutTargets];  // this GPU's flag for (parity, q)
+    uint32_t n, rank;
+    unsigned long long target;
+    int32_t* err;
+};
+
+__device__ __forceinline__ unsigned long long load_acquire_sys(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// One warp. Lane q (q != rank) makes this GPU's output stores of the step
+// visible system-wide, raises this rank's flag on peer q, then waits until
+// peer q has raised its flag here (its rows have landed in this GPU's
+// buffer). A wait longer than kPeerWaitLimitNs records error bit 2 and gives
+// up, so a missing peer never hangs the GPU.
+__global__ void peer_signal_wait(const PeerSignal s) {
+    const uint32_t q = threadIdx.x;
+    if (q >= s.n || q == s.rank) return;
+    __threadfence_system();
+    atomicAdd_system(s.remote[q], 1ull);
+    const uint64_t start = timer_ns();
+    uint32_t spins = 0;
+    while (load_acquire_sys(s.local[q]) < s.target) {
+        if ((++spins & 63u) == 0u && timer_ns() - start > kPeerWaitLimitNs) {
+            if (s.err != nullptr) atomicOr(s.err, 2);
+            return;
+        }
+    }
+}
+
+}  // namespace
+}  // namespace qvp
+
+extern "C" int qvp_peer_group_create(int rank, int nranks, size_t out_bytes, void* handle, qvp_peer_group** group) {
+    if (group == nullptr || handle == nullptr) return fail(QVP_ERR_INVALID, "null argument");
+    if (nranks <= 0 || nranks > kMaxOutTargets || rank < 0 || rank >= nranks)
+        return fail(QVP_ERR_INVALID, "rank %d of %d (at most %d ranks)", rank, nranks, kMaxOutTargets);
+    if (out_bytes == 0) return fail(QVP_ERR_INVALID, "zero output bytes");
+    static_assert(sizeof(cudaIpcMemHandle_t) <= QVP_PEER_HANDLE_BYTES, "IPC handle size");
+    auto* g = new (std::nothrow) qvp_peer_group;
+    if (g == nullptr) return fail(QVP_ERR_NOMEM, "out of host memory");
+    g->rank = rank;
+    g->nranks = nranks;
+    g->out_bytes = out_bytes;
+    g->buf_stride = (out_bytes + 255) / 256 * 256;
+    int rc = check_cuda(cudaGetDevice(&g->device), "cudaGetDevice");
+    const size_t total = 2 * g->buf_stride + 2 * kMaxOutTargets * sizeof(unsigned long long);
+    if (rc == QVP_OK) rc = check_cuda(cudaMalloc(reinterpret_cast<void**>(&g->local), total), "cudaMalloc(peer group)");
+    if (rc == QVP_OK) rc = check_cuda(cudaMemset(g->local, 0, total), "cudaMemset(peer group)");
+    if (rc == QVP_OK) rc = check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(peer group)");
+    cudaIpcMemHandle_t h;
+    if (rc == QVP_OK) rc = check_cuda(cudaIpcGetMemHandle(&h, g->local), "cudaIpcGetMemHandle");
+    if (rc != QVP_OK) {
+        if (g->local != nullptr) cudaFree(g->local);
+        delete g;
+        return rc;
+    }
+    std::memset(handle, 0, QVP_PEER_HANDLE_BYTES);
+    std::memcpy(handle, &h, sizeof(h));
+    g->peer[rank] = g->local;
+    *group = g;
+    return QVP_OK;
+}
+
+extern "C" int qvp_peer_group_open(qvp_peer_group* g, const void* handles) {
+    if (g == nullptr || handles == nullptr) return fail(QVP_ERR_INVALID, "null argument");
+    if (g->opened) return QVP_OK;
+    for (int q = 0; q < g->nranks; ++q) {
+        if (q == g->rank) continue;
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, static_cast<const uint8_t*>(handles) + static_cast<size_t>(q) * QVP_PEER_HANDLE_BYTES,
+                    sizeof(h));
+        void* p = nullptr;
+        const int rc = check_cuda(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+        if (rc != QVP_OK) {
+            for (int k = 0; k < q; ++k)
+                if (k != g->rank && g->peer[k] != nullptr) {
+                    cudaIpcCloseMemHandle(g->peer[k]);
+                    g->peer[k] = nullptr;
+                }
+            return rc;
+        }
+        g->peer[q] = static_cast<uint8_t*>(p);
+    }
+    g->opened = true;
+    return QVP_OK;
+}
+
+extern "C" int qvp_peer_group_destroy(qvp_peer_group* g) {
+    if (g == nullptr) return QVP_OK;
+    cudaDeviceSynchronize();
+    for (int q = 0; q < g->nranks; ++q)
+        if (q != g->rank && g->peer[q] != nullptr) cudaIpcCloseMemHandle(g->peer[q]);
+    if (g->local != nullptr) cudaFree(g->local);
+    cudaGetLastError();
+    delete g;
+    return QVP_OK;
+}
+
+extern "C" void* qvp_peer_group_output(const qvp_peer_group* g, uint64_t step) {
+    return g == nullptr ? nullptr : g->local + (step & 1u) * g->buf_stride;
+}
+
+extern "C" int qvp_shard_decode_peer(const qvp_shard_decode_args* args, qvp_peer_group* g, uint64_t step,
+                                     int32_t* error_word, qvp_stream_t stream) {
+    if (args == nullptr || g == nullptr) return fail(QVP_ERR_INVALID, "null argument");
+    const qvp_shard_decode_args& a = *args;
+    int rc = check_shard(a);
+    if (rc != QVP_OK) return rc;
+    const uint32_t n = a.shard.num_shards;
+    if (static_cast<int>(n) != g->nranks || static_cast<int>(a.shard.shard) != g->rank)
+        return fail(QVP_ERR_INVALID, "peer group is rank %d of %d, shard is %u of %u", g->rank, g->nranks,
+                    a.shard.shard, n);
+    if (n > 1 && !g->opened) return fail(QVP_ERR_INVALID, "peer group not opened");
+    if (a.decode.dtype != QVP_DTYPE_BF16) return fail(QVP_ERR_UNSUPPORTED, "peer output exchange needs bf16");
+    qvp_decode_args d = a.decode;
+    const size_t full = slot_bytes(d) * n;
+    if (full > g->out_bytes)
+        return fail(QVP_ERR_INVALID, "output of %zu bytes does not fit the group's %zu-byte buffers", full,
+                    g->out_bytes);
+    const uint32_t parity = static_cast<uint32_t>(step & 1u);
+    d.out = g->local + parity * g->buf_stride;
+    DecodePlan plan;
+    rc = plan_decode(d, plan);
+    if (rc != QVP_OK || d.batch == 0) return rc;
+    if (!plan.stream) return fail(QVP_ERR_UNSUPPORTED, "peer output exchange needs the stream-K plan");
+    OutTargets t{};
+    t.n = n;
+    t.head0 = a.shard.shard * d.num_query_heads;
+    t.row_heads = d.num_query_heads * n;
+    for (uint32_t q = 0; q < n; ++q)
+        t.ptr[q] = reinterpret_cast<__nv_bfloat16*>(g->peer[q] + parity * g->buf_stride);
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    rc = run_decode(d, plan, st, &t);
+    if (rc != QVP_OK || n == 1) return rc;
+    PeerSignal s{};
+    s.n = n;
+    s.rank = a.shard.shard;
+    s.target = step / 2 + 1;
+    s.err = error_word;
+    for (uint32_t q = 0; q < n; ++q) {
+        if (q == s.rank) continue;
+        s.remote[q] = reinterpret_cast<unsigned long long*>(g->peer[q] + flag_offset(*g, parity, s.rank));
+        s.local[q] = reinterpret_cast<const unsigned long long*>(g->local + flag_offset(*g, parity, q));
+    }
+    peer_signal_wait<<<1, 32, 0, st>>>(s);
+    return check_cuda(cudaGetLastError(), "launch peer_signal_wait");
+}

@@ -113,6 +113,7 @@ class ShardDecodeArgs(C.Structure):
 
 
 NCCL_ID_BYTES = 128
+PEER_HANDLE_BYTES = 64
 
 
 def _load() -> C.CDLL:
@@ -151,6 +152,11 @@ def _load() -> C.CDLL:
         "qvp_nccl_unique_id": (C.c_int, [vp, sz]),
         "qvp_nccl_comm_init": (C.c_int, [vp, sz, C.c_int, C.c_int, P(vp)]),
         "qvp_nccl_comm_destroy": (C.c_int, [vp]),
+        "qvp_peer_group_create": (C.c_int, [C.c_int, C.c_int, sz, vp, P(vp)]),
+        "qvp_peer_group_open": (C.c_int, [vp, vp]),
+        "qvp_peer_group_destroy": (C.c_int, [vp]),
+        "qvp_peer_group_output": (vp, [vp, C.c_uint64]),
+        "qvp_shard_decode_peer": (C.c_int, [P(ShardDecodeArgs), vp, C.c_uint64, vp, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -170,6 +176,8 @@ EXPORTED = [
     "qvp_decode_plan", "qvp_decode", "qvp_decode_noalloc", "qvp_prefill", "qvp_copy_blocks", "qvp_gather_blocks", "qvp_scatter_blocks",
     "qvp_kv_append", "qvp_shard_gather_bytes", "qvp_shard_decode", "qvp_shard_reassemble",
     "qvp_nccl_unique_id", "qvp_nccl_comm_init", "qvp_nccl_comm_destroy",
+    "qvp_peer_group_create", "qvp_peer_group_open", "qvp_peer_group_destroy", "qvp_peer_group_output",
+    "qvp_shard_decode_peer",
 ]
 
 
@@ -277,3 +285,32 @@ def shard_gather_bytes(args: ShardDecodeArgs) -> int:
     n = C.c_size_t()
     check(lib.qvp_shard_gather_bytes(C.byref(args), C.byref(n)), "qvp_shard_gather_bytes")
     return n.value
+
+
+class PeerGroup:
+    """Output exchange over NVLink peer memory for kv-head shards: create on
+    every rank, exchange `handle` (bytes) by any transport, then open with
+    every rank's handle in rank order."""
+
+    def __init__(self, rank: int, nranks: int, out_bytes: int):
+        buf = (C.c_char * PEER_HANDLE_BYTES)()
+        g = C.c_void_p()
+        check(lib.qvp_peer_group_create(rank, nranks, out_bytes, buf, C.byref(g)), "qvp_peer_group_create")
+        self.handle_ptr = g
+        self.handle = bytes(buf)
+
+    def open(self, handles: list) -> None:
+        blob = b"".join(handles)
+        buf = (C.c_char * len(blob)).from_buffer_copy(blob)
+        check(lib.qvp_peer_group_open(self.handle_ptr, buf), "qvp_peer_group_open")
+
+    def output(self, step: int) -> int:
+        return lib.qvp_peer_group_output(self.handle_ptr, step)
+
+    def decode(self, args: ShardDecodeArgs, step: int, error_word: int, stream: int) -> int:
+        return lib.qvp_shard_decode_peer(C.byref(args), self.handle_ptr, step, error_word or None, stream or None)
+
+    def close(self) -> None:
+        if self.handle_ptr:
+            check(lib.qvp_peer_group_destroy(self.handle_ptr), "qvp_peer_group_destroy")
+            self.handle_ptr = None

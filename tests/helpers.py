@@ -152,3 +152,14 @@ class NativeCases:
         msg = C.create_string_buffer(4096)
         rc = getattr(self._lib(), f"{self.prefix}_run")(name.encode(), msg, len(msg))
         return rc, msg.value.decode()
+
+
+def device_bytes(ptr: int, nbytes: int, dev):
+    """A uint8 torch view of `nbytes` of device memory at `ptr` (memory libqvp owns)."""
+    import torch
+
+    class _Raw:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3,
+                                    "strides": None}
+
+    return torch.as_tensor(_Raw(), device=dev)

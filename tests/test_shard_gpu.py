@@ -28,7 +28,7 @@ import oracle
 import qvp
 import sharding
 import workloads as W
-from helpers import gpu_decode
+from helpers import device_bytes, gpu_decode
 
 pytestmark = pytest.mark.gpu
 
@@ -218,6 +218,112 @@ def test_nccl_all_gather_gives_every_rank_every_head(tmp_path):
         p.join(timeout=300)
     alive = [p for p in procs if p.is_alive()]
     for p in alive:  # host processes only: nothing is left running on a GPU
+        p.kill()
+    assert not alive
+    assert [result.get(r) for r in range(world)] == ["ok"] * world
+
+
+# --- output exchange over NVLink peer memory -----------------------------------
+
+def test_peer_group_of_one_gpu_is_qvp_decode_bit_for_bit():
+    import torch
+    dev = torch.device("cuda", 0)
+    w = W.small(55, batch=9, ctx_lo=1, ctx_hi=2500, hq=28, hkv=4, head_dim=128, dtype="bf16")
+    pool, q = W.host_inputs(w)
+    st_u, want, err_u, _ = gpu_decode(w, pool, q)
+    assert st_u == 0 and err_u == 0
+    sw, pool_d, q_d = _shard_inputs(w, pool, q, 1, 0, dev)
+    tab_d = torch.from_numpy(w.tables).to(dev)
+    ctx_d = torch.from_numpy(w.context_lens).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    keep = []
+    a = _decode_args(sw, pool_d, q_d, q_d.data_ptr(), tab_d, ctx_d, err)
+    _with_workspace(a, dev, keep)
+    g = qvp.PeerGroup(0, 1, w.batch * w.num_query_heads * w.head_dim * 2)
+    g.open([g.handle])
+    sa = qvp.shard_decode_args(a, 0, 1, 0, None, 0, 0)
+    st = torch.cuda.current_stream().cuda_stream
+    for step in range(3):
+        assert g.decode(sa, step, err.data_ptr(), st) == 0, qvp.last_error()
+        torch.cuda.synchronize()
+        got = torch.empty((w.batch, w.num_query_heads, w.head_dim), dtype=torch.bfloat16, device=dev)
+        got.view(-1).view(torch.uint8).copy_(device_bytes(g.output(step), got.numel() * 2, dev))
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        assert np.array_equal(got.float().cpu().numpy(), want), step
+    g.close()
+
+
+def _peer_rank_main(rank, world, tmp, result):
+    import time
+
+    import torch
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    w = W.small(56, batch=10, ctx_lo=1, ctx_hi=4000, hq=28, hkv=4, head_dim=128, dtype="bf16")
+    pool, q = W.host_inputs(w)
+    nbytes = w.batch * w.num_query_heads * w.head_dim * 2
+    g = qvp.PeerGroup(rank, world, nbytes)
+    with open(os.path.join(tmp, f"h{rank}.tmp"), "wb") as f:
+        f.write(g.handle)
+    os.rename(os.path.join(tmp, f"h{rank}.tmp"), os.path.join(tmp, f"h{rank}"))
+    t0 = time.time()
+    while not all(os.path.exists(os.path.join(tmp, f"h{r}")) for r in range(world)):
+        if time.time() - t0 > 60:
+            result[rank] = "no handles"
+            return
+        time.sleep(0.05)
+    g.open([open(os.path.join(tmp, f"h{r}"), "rb").read() for r in range(world)])
+    sw, pool_d, q_d = _shard_inputs(w, pool, q, world, rank, dev)
+    tab_d = torch.from_numpy(w.tables).to(dev)
+    ctx_d = torch.from_numpy(w.context_lens).to(dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    keep = []
+    a = _decode_args(sw, pool_d, q_d, q_d.data_ptr(), tab_d, ctx_d, err)
+    _with_workspace(a, dev, keep)
+    sa = qvp.shard_decode_args(a, rank, world, rank, None, 0, 0)
+    st = torch.cuda.current_stream().cuda_stream
+    ref, status = oracle.port_decode(w, pool, q, threads=4)
+    msg = "ok"
+    for step in range(4):  # both buffers, twice
+        rc = g.decode(sa, step, err.data_ptr(), st)
+        if rc != 0:
+            msg = f"qvp_shard_decode_peer {rc}: {qvp.last_error()}"
+            break
+        got = torch.empty((w.batch, w.num_query_heads, w.head_dim), dtype=torch.bfloat16, device=dev)
+        got.view(-1).view(torch.uint8).copy_(device_bytes(g.output(step), nbytes, dev))
+        torch.cuda.synchronize()
+        e = float(np.max(np.abs(got.float().cpu().numpy() - ref)))
+        if int(err.item()) != 0 or not status.all() or e >= BF16_ABS:
+            msg = f"step {step}: err {int(err.item())} max {e}"
+            break
+    torch.cuda.synchronize()
+    # leave only once every rank is done storing into this GPU's buffers
+    with open(os.path.join(tmp, f"done{rank}"), "w") as f:
+        f.write("1")
+    t0 = time.time()
+    while not all(os.path.exists(os.path.join(tmp, f"done{r}")) for r in range(world)) and time.time() - t0 < 120:
+        time.sleep(0.05)
+    g.close()
+    result[rank] = msg
+
+
+def test_peer_exchange_gives_every_rank_every_head(tmp_path):
+    import torch
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 4)
+    if world < 2:
+        pytest.skip("needs two GPUs")
+    mgr = mp.Manager()
+    result = mgr.dict()
+    ctx = mp.get_context("spawn")
+    procs = [ctx.Process(target=_peer_rank_main, args=(r, world, str(tmp_path), result)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:  # host processes only: every GPU wait in the kernels is bounded
         p.kill()
     assert not alive
     assert [result.get(r) for r in range(world)] == ["ok"] * world
