@@ -640,10 +640,13 @@ def run_scenario(args):
         rc = lib.qvp_scenario_cow(16, 8, 2048, 64, 3, max(args.steps, 1), buf, len(buf))
         metric, key, unit = "copy-on-write materialisation, batched copy kernel GB/s (read+write)", "cow_gbs", "GB/s"
     else:
-        lib.qvp_scenario_swap.argtypes = [C.c_uint32, C.c_double, C.c_double, C.c_int, C.c_int, C.c_char_p,
-                                          C.c_size_t]
-        rc = lib.qvp_scenario_swap(args.swap_pool_blocks, 0.9, 0.25, 64, 5, buf, len(buf))
-        metric, key, unit = "swap-out GB/s to pinned host memory (gather kernel + cudaMemcpyAsync)", "swap_out_gbs", "GB/s"
+        lib.qvp_scenario_swap.argtypes = [C.c_uint32, C.c_double, C.c_double, C.c_int, C.c_int, C.c_int,
+                                          C.c_char_p, C.c_size_t]
+        coded = args.swap_coding == "compressed"
+        rc = lib.qvp_scenario_swap(args.swap_pool_blocks, 0.9, 0.25, 64, 5, int(coded), buf, len(buf))
+        how = ("compress kernel writing coded slots to mapped pinned memory" if coded
+               else "gather kernel + cudaMemcpyAsync")
+        metric, key, unit = f"swap-out GB/s of block bytes to pinned host memory ({how})", "swap_out_gbs", "GB/s"
     if rc < 0:
         raise SystemExit("scenario output overflow")
     d = json.loads(buf.value.decode())
@@ -827,6 +830,8 @@ def main():
     p.add_argument("--prefill-cpu-positions", type=int, default=512,
                    help="prefill: positions in the CPU baseline sample")
     p.add_argument("--swap-pool-blocks", type=int, default=1 << 20, help="cfg5 pool size in 64 KiB blocks")
+    p.add_argument("--swap-coding", choices=["raw", "compressed"], default="raw",
+                   help="cfg5: swap slots verbatim or coded (lossless) by the device")
     p.add_argument("--split", type=int, default=0, help="split-K partition in tokens (0 = auto)")
     p.add_argument("--cpu-budget", type=float, default=15.0, help="seconds of CPU-baseline timing")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")

@@ -251,6 +251,52 @@ QVP_API int qvp_scatter_blocks(void* pool, size_t block_stride, uint32_t num_blo
                        const void* staging, int32_t* error_word, qvp_stream_t stream);
 
 /* ---------------------------------------------------------------------------
+ * qvp_fetch_host: copy `bytes` from page-locked host memory (mapped into the
+ * device's address space, as all page-locked memory is under unified
+ * addressing) to device memory with a kernel whose SMs read over PCIe. The
+ * engine's small per-step uploads (block tables, copy pairs, append slots)
+ * go this way so that they never wait behind a large swap copy queued on the
+ * copy engines. The host must not change `src` until the kernel has run.
+ * ------------------------------------------------------------------------- */
+QVP_API int qvp_fetch_host(void* dst, const void* src, size_t bytes, qvp_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Compressed swap slots (lossless). The reference's swap path copies every
+ * block's bytes verbatim (src/SwapBackend.cpp:10-39) and names compressing
+ * swapped blocks as the way to cut link time (docs/architecture.md:128-130).
+ *
+ * qvp_compress_blocks codes block ids[i] of the pool, for i < n, into swap
+ * slot slots[i]; qvp_decompress_blocks is the inverse. A slot is split in
+ * two places: its first head_bytes bytes at heads + i*head_bytes (indexed by
+ * list position: a device staging buffer that the caller moves with the copy
+ * engines) and the rest at tails + slots[i]*tail_stride (normally pinned
+ * host memory mapped into the device, which the kernels reach over PCIe).
+ * head_bytes = 0 puts whole slots in the tails. A slot holds a 16-byte
+ * header (u32 format 'QVP1' coded / 'QVP0' raw, u32 escapes, u32 bytes used,
+ * u32 0) and then either the raw block or, for bf16 blocks: a 16-byte
+ * dictionary of the 15 most frequent high bytes, one 4-bit code per value
+ * (code 15 = escape), the low bytes, and u32 escapes (value index << 8 |
+ * high byte). Blocks that would not shrink are stored raw. Requirements:
+ * head_bytes + tail_stride >= qvp_swap_slot_bytes(block_bytes); block_bytes,
+ * head_bytes, tail_stride and the stride multiples of 16; pool, heads and
+ * tails 16-byte aligned. `bytes_moved` (device u64[2], optional) accumulates
+ * the slot bytes used and, of those, the bytes past head_bytes. Ids or slots
+ * out of range are skipped and recorded in *error_word (1), as are slots
+ * this codec did not write (the frame is left as it was).
+ * ------------------------------------------------------------------------- */
+QVP_API size_t qvp_swap_slot_bytes(size_t block_bytes);
+QVP_API int qvp_compress_blocks(const void* pool, size_t block_stride, uint32_t num_blocks,
+                        size_t block_bytes, const int32_t* ids, const int32_t* slots, uint32_t n,
+                        void* heads, size_t head_bytes, void* tails, size_t tail_stride,
+                        uint32_t num_slots, unsigned long long* bytes_moved, int32_t* error_word,
+                        qvp_stream_t stream);
+QVP_API int qvp_decompress_blocks(void* pool, size_t block_stride, uint32_t num_blocks,
+                          size_t block_bytes, const int32_t* ids, const int32_t* slots, uint32_t n,
+                          const void* heads, size_t head_bytes, const void* tails, size_t tail_stride,
+                          uint32_t num_slots, unsigned long long* bytes_moved, int32_t* error_word,
+                          qvp_stream_t stream);
+
+/* ---------------------------------------------------------------------------
  * KV append: write one new token's K and V for every kv head of every
  * sequence: for b < batch, token position positions[b] of sequence b goes to
  * block block_tables[b*pitch + pos/tokens_per_block], slot pos%tokens_per_block,

@@ -183,3 +183,78 @@ def port_prefill(w, pool, q, query_lens, threads=1):
     o, status = port_decode(w, pool, qq, threads=threads, context_lens=ctx, tables=tables)
     out[seq, tok] = o
     return out, status
+
+
+# ---- compressed swap slots ----------------------------------------------------
+# The reference stores a swapped block's bytes verbatim
+# (src/SwapBackend.cpp:10-39); a compressed slot must give back exactly those
+# bytes. The slot format (header, 4-bit high-byte codes over a 15-entry
+# dictionary, raw low bytes, u32 escapes) is restated here in numpy so the
+# tests can check the device coder byte for byte, not only by round trip.
+
+SLOT_CODED = 0x31505651  # "QVP1"
+SLOT_RAW = 0x30505651    # "QVP0"
+
+
+def swap_slot_bytes(block_bytes: int) -> int:
+    return (block_bytes + 16 + 15) // 16 * 16
+
+
+def port_compress_block(block: np.ndarray) -> tuple[np.ndarray, set]:
+    """Codes one block (uint8 array). Returns (slot bytes of length
+    swap_slot_bytes, set of escape words). The escape list's order is free in
+    the format (the device coder appends them as they are found); this one
+    writes them in index order and also returns them as a set."""
+    nb = block.size
+    slot = np.zeros(swap_slot_bytes(nb), dtype=np.uint8)
+    n = nb // 2
+    codable = nb % 32 == 0 and n < (1 << 24)
+    escapes: set = set()
+    if codable:
+        vals = block.view(np.uint16)
+        hi = (vals >> 8).astype(np.int64)
+        lo = (vals & 0xFF).astype(np.uint8)
+        hist = np.bincount(hi, minlength=256)
+        # rank by count descending, ties to the smaller byte
+        order = sorted(range(256), key=lambda u: (-hist[u], u))
+        code_of = np.full(256, 15, dtype=np.uint8)
+        dictionary = np.zeros(16, dtype=np.uint8)
+        for r, u in enumerate(order[:15]):
+            if hist[u] > 0:
+                code_of[u] = r
+                dictionary[r] = u
+        codes = code_of[hi]
+        esc_idx = np.nonzero(codes == 15)[0]
+        used = 32 + n * 3 // 2 + 4 * len(esc_idx)
+        if used < 16 + nb:
+            slot[:16] = np.array([SLOT_CODED, len(esc_idx), used, 0], dtype=np.uint32).view(np.uint8)
+            slot[16:32] = dictionary
+            slot[32:32 + n // 2] = (codes[0::2] | (codes[1::2] << 4)).astype(np.uint8)
+            slot[32 + n // 2:32 + n * 3 // 2] = lo
+            words = (esc_idx.astype(np.uint32) << 8) | hi[esc_idx].astype(np.uint32)
+            e0 = 32 + n * 3 // 2
+            slot[e0:e0 + 4 * len(words)] = words.view(np.uint8)
+            return slot, {int(x) for x in words}
+    slot[:16] = np.array([SLOT_RAW, 0, 16 + nb, 0], dtype=np.uint32).view(np.uint8)
+    slot[16:16 + nb] = block
+    return slot, escapes
+
+
+def port_decompress_slot(slot: np.ndarray, block_bytes: int) -> np.ndarray:
+    """The block a slot codes (uint8 array of block_bytes)."""
+    head = slot[:16].view(np.uint32)
+    if head[0] == SLOT_RAW:
+        return slot[16:16 + block_bytes].copy()
+    assert head[0] == SLOT_CODED, "not a swap slot"
+    n = block_bytes // 2
+    dictionary = slot[16:32]
+    packed = slot[32:32 + n // 2]
+    codes = np.empty(n, dtype=np.uint8)
+    codes[0::2] = packed & 15
+    codes[1::2] = packed >> 4
+    hi = np.where(codes < 15, dictionary[np.minimum(codes, 14)], 0).astype(np.uint16)
+    lo = slot[32 + n // 2:32 + n * 3 // 2].astype(np.uint16)
+    out = (hi << 8) | lo
+    esc = slot[32 + n * 3 // 2:32 + n * 3 // 2 + 4 * int(head[1])].view(np.uint32)
+    out[esc >> 8] = ((esc & 0xFF).astype(np.uint16) << 8) | lo[esc >> 8]
+    return out.view(np.uint8).copy()

@@ -104,6 +104,22 @@ __global__ void __launch_bounds__(kMoverThreads) kv_append_kernel(uint8_t* pool,
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Device <- mapped pinned host memory by SM loads over PCIe.
+__global__ void __launch_bounds__(kMoverThreads) fetch_host_kernel(uint8_t* __restrict__ dst,
+                                                                   const uint8_t* __restrict__ src, size_t bytes,
+                                                                   bool vec) {
+    const size_t first = static_cast<size_t>(blockIdx.x) * kMoverThreads + threadIdx.x;
+    const size_t step = static_cast<size_t>(gridDim.x) * kMoverThreads;
+    if (vec) {
+        const size_t nv = bytes / 16;
+        for (size_t i = first; i < nv; i += step)
+            reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+        for (size_t i = nv * 16 + first; i < bytes; i += step) dst[i] = src[i];
+    } else {
+        for (size_t i = first; i < bytes; i += step) dst[i] = src[i];
+    }
+}
+
 }  // namespace
 
 }  // namespace qvp
@@ -152,6 +168,17 @@ extern "C" int qvp_scatter_blocks(void* pool, size_t block_stride, uint32_t num_
                                   qvp_stream_t stream) {
     return launch_move(pool, block_stride, num_blocks, bytes, ids, n, const_cast<void*>(staging), error_word,
                        stream, false);
+}
+
+extern "C" int qvp_fetch_host(void* dst, const void* src, size_t bytes, qvp_stream_t stream) {
+    if (bytes == 0) return QVP_OK;
+    if (dst == nullptr || src == nullptr) return fail(QVP_ERR_INVALID, "null destination or source");
+    const bool vec = aligned16(dst) && aligned16(src);
+    const size_t per_cta = static_cast<size_t>(kMoverThreads) * (vec ? 16 : 1) * 4;
+    const size_t ctas = std::min<size_t>((bytes + per_cta - 1) / per_cta, 2 * 148);
+    fetch_host_kernel<<<static_cast<unsigned>(ctas), kMoverThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint8_t*>(dst), static_cast<const uint8_t*>(src), bytes, vec);
+    return check_cuda(cudaGetLastError(), "launch fetch_host");
 }
 
 extern "C" int qvp_kv_append(void* pool, size_t block_stride, uint32_t num_blocks, const qvp_block_shape* shape,

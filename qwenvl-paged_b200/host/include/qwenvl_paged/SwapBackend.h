@@ -18,6 +18,7 @@
 #include <set>
 #include <string>
 #include <unordered_map>
+#include <utility>
 #include <vector>
 
 struct CUstream_st;
@@ -92,9 +93,22 @@ private:
 // lists, the copy stream and its events) is allocated at construction, so a
 // move once recorded is never dropped; if any of it cannot be had, ready() is
 // false and every store is refused, leaving the bookkeeping untouched.
+//
+// With SwapCoding::compressed a flush codes the stored blocks on the copy
+// stream (qvp_compress_blocks) into device staging and the copy engines move
+// only each slot's head (the coded form of a K/V block, about 0.755 of its
+// bytes) to the slab; the rare slot longer than its head (a block stored raw,
+// or one with many escapes) has its tail written by the kernel itself into
+// mapped pinned memory. Loads run the same way back (qvp_decompress_blocks).
+// The bytes a load gives back are exactly those stored. The coding kernels
+// take SM time that plain copies do not; they run one short CTA per block on
+// a stream of the lowest priority, so a decode launched meanwhile gets SMs
+// first.
+enum class SwapCoding { raw, compressed };
+
 class DeviceSwapBackend final : public SwapBackend {
 public:
-    DeviceSwapBackend(MemoryAllocator& allocator, std::size_t max_slots);
+    DeviceSwapBackend(MemoryAllocator& allocator, std::size_t max_slots, SwapCoding coding = SwapCoding::raw);
     ~DeviceSwapBackend() override;
     DeviceSwapBackend(const DeviceSwapBackend&) = delete;
     DeviceSwapBackend& operator=(const DeviceSwapBackend&) = delete;
@@ -112,12 +126,18 @@ public:
     // False when a buffer of the backend could not be allocated (every store
     // is refused).
     [[nodiscard]] bool ready() const noexcept;
-    // Host address of a resident slot's bytes (for tests), null if unknown.
+    // Host address of a resident slot's bytes (compressed: of its head), null
+    // if unknown.
     // Valid once wait_idle() has returned after the flush that filled it.
     [[nodiscard]] const std::byte* slot_bytes(SwapSlotId slot) const noexcept;
-    // Bytes moved between pool and slab so far, in each direction.
+    // Block bytes moved between pool and slab so far, in each direction.
     [[nodiscard]] std::uint64_t bytes_out() const noexcept { return bytes_out_; }
     [[nodiscard]] std::uint64_t bytes_in() const noexcept { return bytes_in_; }
+    [[nodiscard]] SwapCoding coding() const noexcept { return coding_; }
+    // Bytes that crossed the host link so far, {out, in}: the coded slot
+    // bytes with SwapCoding::compressed, the block bytes otherwise. Waits
+    // (bounded) for the moves enqueued so far.
+    [[nodiscard]] std::pair<std::uint64_t, std::uint64_t> link_bytes();
     // The copy stream the moves run on.
     [[nodiscard]] CUstream_st* copy_stream() const noexcept { return copy_; }
     // Text of the first failure (a launch error or a timed-out wait); empty
@@ -129,18 +149,25 @@ private:
         std::int32_t block;
         std::uint32_t slab_index;
     };
-    void flush_moves(std::vector<Move>& moves, bool stores, std::int32_t* ids_dev);
+    void flush_moves(std::vector<Move>& moves, bool stores, std::int32_t* ids_dev, std::int32_t* slab_idx_dev);
     void note(const std::string& what);  // keeps the first error
     void refresh_loads() const;
 
     MemoryAllocator* allocator_{nullptr};
     std::size_t max_slots_{0};
-    std::size_t slot_bytes_{0};
-    std::byte* slab_{nullptr};            // pinned host, max_slots * slot_bytes
-    std::byte* staging_{nullptr};         // device, staging_blocks_ * slot_bytes
+    std::size_t slot_bytes_{0};           // bytes of one block
+    SwapCoding coding_{SwapCoding::raw};
+    std::size_t slab_stride_{0};          // bytes of one slab slot (compressed: of its head)
+    std::size_t tail_stride_{0};          // compressed: bytes of a slot past its head
+    std::byte* slab_{nullptr};            // pinned host, max_slots * slab_stride (+ tails)
+    std::byte* tails_dev_{nullptr};       // compressed: device address of the mapped tails
+    unsigned long long* link_dev_{nullptr};  // compressed: device {out used, out tail, in used, in tail}
+    std::uint64_t heads_out_{0};          // compressed: head bytes moved by the copy engines
+    std::uint64_t heads_in_{0};
+    std::byte* staging_{nullptr};         // device, staging_blocks_ * slab_stride
     std::size_t staging_blocks_{0};
-    // two block-id lists (pinned + device) of 2 * max_slots entries; flushes
-    // alternate between them
+    // two move lists (pinned + device) of 2 * max_slots block ids, followed
+    // (compressed) by as many slab indices; flushes alternate between them
     std::int32_t* ids_host_[2]{nullptr, nullptr};
     std::int32_t* ids_dev_[2]{nullptr, nullptr};
     CUevent_st* ids_uploaded_[2]{nullptr, nullptr};  // the list's last upload

@@ -85,7 +85,7 @@ void upload(MemoryAllocator& alloc, const std::vector<std::int32_t>& staged, std
     std::memcpy(host, staged.data(), staged.size() * sizeof(std::int32_t));
     alloc.flush();
     alloc.order_writes();
-    cudaMemcpyAsync(dev, host, staged.size() * sizeof(std::int32_t), cudaMemcpyHostToDevice, alloc.stream());
+    host_impl::upload_pinned(dev, host, staged.size() * sizeof(std::int32_t), alloc.stream());
     cudaEventRecord(static_cast<cudaEvent_t>(event), alloc.stream());
 }
 

@@ -195,7 +195,7 @@ void MemoryAllocator::flush_copies() {
     // the pinned list of the previous flush must have reached the device
     if (!host_impl::wait_event(static_cast<cudaEvent_t>(pairs_event_), "copy-pair upload", &error_)) return;
     std::memcpy(pairs_host_, pending_pairs_.data(), n * sizeof(std::int32_t));
-    cudaMemcpyAsync(pairs_dev_, pairs_host_, n * sizeof(std::int32_t), cudaMemcpyHostToDevice, stream_);
+    host_impl::upload_pinned(pairs_dev_, pairs_host_, n * sizeof(std::int32_t), stream_);
     cudaEventRecord(static_cast<cudaEvent_t>(pairs_event_), stream_);
     const int rc = qvp_copy_blocks(pool_, stride_, config_.max_blocks, blocks_.empty() ? 0 : blocks_[0]->size_bytes(),
                                    pairs_dev_, static_cast<std::uint32_t>(n / 2), nullptr, stream_);

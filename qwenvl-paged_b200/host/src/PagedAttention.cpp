@@ -219,7 +219,7 @@ bool PagedDecodeBatch::run(const std::vector<CacheView>& views, const std::vecto
     alloc.flush();  // queued copy-on-write copies and swap moves land first
     alloc.order_reads(host_buf_, B * pitch);  // swap-ins still filling a frame of the batch
     cudaStream_t st = alloc.stream();
-    cudaMemcpyAsync(dev_buf_, host_buf_, ints * sizeof(std::int32_t), cudaMemcpyHostToDevice, st);
+    host_impl::upload_pinned(dev_buf_, host_buf_, ints * sizeof(std::int32_t), st);
     cudaEventRecord(static_cast<cudaEvent_t>(upload_event_), st);
     rows_uploaded_ = static_cast<std::uint32_t>(B);
     bytes_uploaded_ = ints * sizeof(std::int32_t);

@@ -195,14 +195,16 @@ bool ResidentBlockTables::update(const std::vector<CacheView>& views, const std:
     }
     cudaStream_t st = allocator_->stream();
     // the previous step's upload must have left the pinned buffer
-    cudaEventSynchronize(static_cast<cudaEvent_t>(upload_event_));
+    if (!host_impl::wait_event(static_cast<cudaEvent_t>(upload_event_), "resident table upload", why)) {
+        planner_.invalidate();
+        status_ = QVP_ERR_CUDA;
+        return false;
+    }
     std::memcpy(packet_host_, pk.data(), pk.size() * sizeof(std::int32_t));
     const std::size_t bytes = pk.size() * sizeof(std::int32_t);
     const std::uint32_t n = planner_.rows_written();
     const std::size_t row_bytes = static_cast<std::size_t>(planner_.pitch()) * sizeof(std::int32_t);
-    int status = cudaMemcpyAsync(packet_dev_, packet_host_, bytes, cudaMemcpyHostToDevice, st) == cudaSuccess
-                     ? QVP_OK
-                     : QVP_ERR_CUDA;
+    int status = host_impl::upload_pinned(packet_dev_, packet_host_, bytes, st) ? QVP_OK : QVP_ERR_CUDA;
     cudaEventRecord(static_cast<cudaEvent_t>(upload_event_), st);
     // qvp_scatter_blocks takes at most 65535 rows per launch
     for (std::uint32_t first = 0; status == QVP_OK && first < n; first += 65535u) {

@@ -95,28 +95,55 @@ void for_each_run(const std::uint32_t* idx, std::size_t n, Fn fn) {
 
 }  // namespace
 
-DeviceSwapBackend::DeviceSwapBackend(MemoryAllocator& allocator, std::size_t max_slots)
-    : allocator_(&allocator), max_slots_(max_slots) {
+DeviceSwapBackend::DeviceSwapBackend(MemoryAllocator& allocator, std::size_t max_slots, SwapCoding coding)
+    : allocator_(&allocator), max_slots_(max_slots), coding_(coding) {
     const PhysicalBlock* b0 = allocator.block(0);
     slot_bytes_ = b0 != nullptr ? b0->size_bytes() : 0;
     if (!allocator.has_storage() || slot_bytes_ == 0 || max_slots_ == 0) return;
     OnDevice guard(allocator.device());
+    const bool coded = coding_ == SwapCoding::compressed;
+    if (coded && slot_bytes_ % 16 != 0) {
+        note("swap backend: compressed slots need blocks of a multiple of 16 bytes; every store is refused");
+        return;
+    }
+    if (coded) {
+        // a slot's head holds a coded block with up to one escape per 512
+        // values; longer slots spill into the mapped tail
+        const std::size_t full = qvp_swap_slot_bytes(slot_bytes_);
+        const std::size_t head = (32 + slot_bytes_ / 4 * 3 + slot_bytes_ / 256 + 15) / 16 * 16;
+        slab_stride_ = slot_bytes_ % 32 == 0 ? std::min(head, full) : full;
+        tail_stride_ = full - slab_stride_;
+    } else {
+        slab_stride_ = slot_bytes_;
+    }
     // Everything a flush needs is allocated here, so recorded moves always run.
     const std::size_t staging = std::min<std::size_t>(
-        max_slots_, std::min<std::size_t>(65535, std::max<std::size_t>(1, kMaxStagingBytes / slot_bytes_)));
-    const std::size_t id_entries = 2 * max_slots_;
+        max_slots_, std::min<std::size_t>(65535, std::max<std::size_t>(1, kMaxStagingBytes / slab_stride_)));
+    const std::size_t id_entries = (coded ? 4 : 2) * max_slots_;
     void* p = nullptr;
-    bool ok = cudaHostAlloc(&p, max_slots_ * slot_bytes_, cudaHostAllocDefault) == cudaSuccess;
+    bool ok = cudaHostAlloc(&p, max_slots_ * (slab_stride_ + tail_stride_),
+                            coded ? cudaHostAllocMapped : cudaHostAllocDefault) == cudaSuccess;
     if (ok) slab_ = static_cast<std::byte*>(p);
-    ok = ok && cudaMalloc(reinterpret_cast<void**>(&staging_), staging * slot_bytes_) == cudaSuccess;
+    if (coded) {
+        void* d = nullptr;
+        ok = ok && cudaHostGetDevicePointer(&d, slab_, 0) == cudaSuccess;
+        tails_dev_ = static_cast<std::byte*>(d) + max_slots_ * slab_stride_;
+        ok = ok && cudaMalloc(reinterpret_cast<void**>(&link_dev_), 4 * sizeof(unsigned long long)) == cudaSuccess &&
+             cudaMemset(link_dev_, 0, 4 * sizeof(unsigned long long)) == cudaSuccess;
+    }
+    ok = ok && cudaMalloc(reinterpret_cast<void**>(&staging_), staging * slab_stride_) == cudaSuccess;
     for (int b = 0; ok && b < 2; ++b) {
         ok = cudaMallocHost(reinterpret_cast<void**>(&ids_host_[b]), id_entries * sizeof(std::int32_t)) ==
                  cudaSuccess &&
              cudaMalloc(reinterpret_cast<void**>(&ids_dev_[b]), id_entries * sizeof(std::int32_t)) == cudaSuccess &&
              make_event(ids_uploaded_[b]);
     }
+    // the lowest priority: the block scheduler serves a decode launched
+    // meanwhile before the swap's gather, scatter or coding CTAs
+    int least = 0, greatest = 0;
+    cudaDeviceGetStreamPriorityRange(&least, &greatest);
     cudaStream_t cs = nullptr;
-    ok = ok && cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking) == cudaSuccess;
+    ok = ok && cudaStreamCreateWithPriority(&cs, cudaStreamNonBlocking, least) == cudaSuccess;
     if (ok) copy_ = cs;
     ok = ok && make_event(engine_mark_) && make_event(moves_done_);
     if (!ok) {
@@ -135,6 +162,7 @@ DeviceSwapBackend::~DeviceSwapBackend() {
     if (copy_ != nullptr) host_impl::wait_stream(copy_, "swap backend teardown", nullptr);
     if (slab_ != nullptr) cudaFreeHost(slab_);
     if (staging_ != nullptr) cudaFree(staging_);
+    if (link_dev_ != nullptr) cudaFree(link_dev_);
     for (int b = 0; b < 2; ++b) {
         if (ids_dev_[b] != nullptr) cudaFree(ids_dev_[b]);
         if (ids_host_[b] != nullptr) cudaFreeHost(ids_host_[b]);
@@ -155,7 +183,20 @@ std::size_t DeviceSwapBackend::resident_slots() const noexcept { return slots_.s
 
 const std::byte* DeviceSwapBackend::slot_bytes(SwapSlotId slot) const noexcept {
     const auto it = slots_.find(slot);
-    return it == slots_.end() ? nullptr : slab_ + static_cast<std::size_t>(it->second) * slot_bytes_;
+    return it == slots_.end() ? nullptr : slab_ + static_cast<std::size_t>(it->second) * slab_stride_;
+}
+
+std::pair<std::uint64_t, std::uint64_t> DeviceSwapBackend::link_bytes() {
+    if (coding_ != SwapCoding::compressed || link_dev_ == nullptr) return {bytes_out_, bytes_in_};
+    unsigned long long v[4] = {0, 0, 0, 0};
+    if (!wait_idle()) return {0, 0};
+    OnDevice guard(allocator_->device());
+    if (cudaMemcpyAsync(v, link_dev_, sizeof v, cudaMemcpyDeviceToHost, copy_) != cudaSuccess ||
+        !host_impl::wait_stream(copy_, "swap link byte counters", &error_)) {
+        cudaGetLastError();
+        return {0, 0};
+    }
+    return {heads_out_ + v[1], heads_in_ + v[3]};
 }
 
 std::optional<SwapSlotId> DeviceSwapBackend::store(const PhysicalBlock& block) {
@@ -180,7 +221,9 @@ bool DeviceSwapBackend::load(SwapSlotId slot, PhysicalBlock& block) {
     if (it == slots_.end() || block.size_bytes() < slot_bytes_) return false;
     if (block.data() != allocator_->pool_base() + static_cast<std::size_t>(block.id()) * allocator_->block_stride())
         return false;
-    if (!pending_stores_.empty()) flush();
+    // stores and loads keep their program order; a flush carries at most
+    // max_slots moves, the size of its id lists
+    if (!pending_stores_.empty() || pending_loads_.size() >= max_slots_) flush();
     pending_loads_.push_back({static_cast<std::int32_t>(block.id()), it->second});
     return true;
 }
@@ -212,15 +255,25 @@ void DeviceSwapBackend::flush() {
     const int b = ids_next_;
     ids_next_ ^= 1;
     if (!host_impl::wait_event(ev(ids_uploaded_[b]), "swap flush: id list still uploading", &error_)) return;
-    std::size_t n = 0;
-    for (const Move& m : pending_stores_) ids_host_[b][n++] = m.block;
-    for (const Move& m : pending_loads_) ids_host_[b][n++] = m.block;
-    cudaMemcpyAsync(ids_dev_[b], ids_host_[b], n * sizeof(std::int32_t), cudaMemcpyHostToDevice, copy_);
+    const bool coded = coding_ == SwapCoding::compressed;
+    const std::size_t n = pending_stores_.size() + pending_loads_.size();
+    std::size_t k = 0;
+    for (const Move& m : pending_stores_) {
+        if (coded) ids_host_[b][n + k] = static_cast<std::int32_t>(m.slab_index);
+        ids_host_[b][k++] = m.block;
+    }
+    for (const Move& m : pending_loads_) {
+        if (coded) ids_host_[b][n + k] = static_cast<std::int32_t>(m.slab_index);
+        ids_host_[b][k++] = m.block;
+    }
+    cudaMemcpyAsync(ids_dev_[b], ids_host_[b], (coded ? 2 * n : n) * sizeof(std::int32_t), cudaMemcpyHostToDevice,
+                    copy_);
     cudaEventRecord(ev(ids_uploaded_[b]), copy_);
     ++flush_seq_;
     const bool loads = !pending_loads_.empty();
-    flush_moves(pending_stores_, true, ids_dev_[b]);
-    flush_moves(pending_loads_, false, ids_dev_[b] + (n - pending_loads_.size()));
+    const std::size_t ns = pending_stores_.size();
+    flush_moves(pending_stores_, true, ids_dev_[b], ids_dev_[b] + n);
+    flush_moves(pending_loads_, false, ids_dev_[b] + ns, ids_dev_[b] + n + ns);
     cudaEventRecord(ev(moves_done_), copy_);
     if (loads) last_load_flush_ = flush_seq_;
     pending_stores_.clear();
@@ -230,8 +283,11 @@ void DeviceSwapBackend::flush() {
 }
 
 // Enqueues `moves` on the copy stream in chunks of the staging size; ids_dev
-// already holds their block ids in order.
-void DeviceSwapBackend::flush_moves(std::vector<Move>& moves, bool stores, std::int32_t* ids_dev) {
+// already holds their block ids in order and slab_idx_dev (compressed) their
+// slab indices. A chunk is a gather (or coding) kernel into staging plus one
+// copy per run of consecutive slab slots; loads the reverse.
+void DeviceSwapBackend::flush_moves(std::vector<Move>& moves, bool stores, std::int32_t* ids_dev,
+                                    std::int32_t* slab_idx_dev) {
     if (moves.empty()) return;
     std::vector<std::uint32_t> idx(moves.size());
     for (std::size_t i = 0; i < moves.size(); ++i) idx[i] = moves[i].slab_index;
@@ -239,29 +295,44 @@ void DeviceSwapBackend::flush_moves(std::vector<Move>& moves, bool stores, std::
         if (frame_load_flush_.size() < allocator_->num_blocks()) frame_load_flush_.resize(allocator_->num_blocks(), 0);
         for (const Move& m : moves) frame_load_flush_[static_cast<std::size_t>(m.block)] = flush_seq_;
     }
+    const bool coded = coding_ == SwapCoding::compressed;
+    const auto slots = static_cast<std::uint32_t>(max_slots_);
     for (std::size_t base = 0; base < moves.size(); base += staging_blocks_) {
         const std::size_t n = std::min(staging_blocks_, moves.size() - base);
+        const auto n32 = static_cast<std::uint32_t>(n);
         if (stores) {
-            if (qvp_gather_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(),
-                                  slot_bytes_, ids_dev + base, static_cast<std::uint32_t>(n), staging_, nullptr,
-                                  copy_) != QVP_OK)
-                note(std::string("swap-out gather: ") + qvp_last_error());
+            const int rc =
+                coded ? qvp_compress_blocks(allocator_->pool_base(), allocator_->block_stride(),
+                                            allocator_->num_blocks(), slot_bytes_, ids_dev + base,
+                                            slab_idx_dev + base, n32, staging_, slab_stride_, tails_dev_,
+                                            tail_stride_, slots, link_dev_, nullptr, copy_)
+                      : qvp_gather_blocks(allocator_->pool_base(), allocator_->block_stride(),
+                                          allocator_->num_blocks(), slot_bytes_, ids_dev + base, n32, staging_,
+                                          nullptr, copy_);
+            if (rc != QVP_OK) note(std::string(coded ? "swap-out compress: " : "swap-out gather: ") + qvp_last_error());
             for_each_run(idx.data() + base, n, [&](std::size_t first, std::size_t count) {
-                copy_in_pieces(slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
-                               staging_ + first * slot_bytes_, count * slot_bytes_, cudaMemcpyDeviceToHost, copy_);
+                copy_in_pieces(slab_ + static_cast<std::size_t>(idx[base + first]) * slab_stride_,
+                               staging_ + first * slab_stride_, count * slab_stride_, cudaMemcpyDeviceToHost, copy_);
             });
             bytes_out_ += n * slot_bytes_;
+            if (coded) heads_out_ += n * slab_stride_;
         } else {
             for_each_run(idx.data() + base, n, [&](std::size_t first, std::size_t count) {
-                copy_in_pieces(staging_ + first * slot_bytes_,
-                               slab_ + static_cast<std::size_t>(idx[base + first]) * slot_bytes_,
-                               count * slot_bytes_, cudaMemcpyHostToDevice, copy_);
+                copy_in_pieces(staging_ + first * slab_stride_,
+                               slab_ + static_cast<std::size_t>(idx[base + first]) * slab_stride_,
+                               count * slab_stride_, cudaMemcpyHostToDevice, copy_);
             });
-            if (qvp_scatter_blocks(allocator_->pool_base(), allocator_->block_stride(), allocator_->num_blocks(),
-                                   slot_bytes_, ids_dev + base, static_cast<std::uint32_t>(n), staging_, nullptr,
-                                   copy_) != QVP_OK)
-                note(std::string("swap-in scatter: ") + qvp_last_error());
+            const int rc =
+                coded ? qvp_decompress_blocks(allocator_->pool_base(), allocator_->block_stride(),
+                                              allocator_->num_blocks(), slot_bytes_, ids_dev + base,
+                                              slab_idx_dev + base, n32, staging_, slab_stride_, tails_dev_,
+                                              tail_stride_, slots, link_dev_ + 2, nullptr, copy_)
+                      : qvp_scatter_blocks(allocator_->pool_base(), allocator_->block_stride(),
+                                           allocator_->num_blocks(), slot_bytes_, ids_dev + base, n32, staging_,
+                                           nullptr, copy_);
+            if (rc != QVP_OK) note(std::string(coded ? "swap-in decompress: " : "swap-in scatter: ") + qvp_last_error());
             bytes_in_ += n * slot_bytes_;
+            if (coded) heads_in_ += n * slab_stride_;
         }
     }
 }

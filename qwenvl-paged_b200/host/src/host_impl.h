@@ -35,6 +35,16 @@ struct OnDevice {
     }
 };
 
+// Uploads a small pinned host buffer to the device on `st`. Up to
+// kFetchLimit bytes the SMs read it over PCIe (qvp_fetch_host), so the upload
+// does not queue behind swap copies on the copy engines; larger ones go by
+// cudaMemcpyAsync.
+constexpr std::size_t kFetchLimit = std::size_t(4) << 20;
+inline bool upload_pinned(void* dev, const void* pinned, std::size_t bytes, cudaStream_t st) {
+    if (bytes <= kFetchLimit) return qvp_fetch_host(dev, pinned, bytes, st) == QVP_OK;
+    return cudaMemcpyAsync(dev, pinned, bytes, cudaMemcpyHostToDevice, st) == cudaSuccess;
+}
+
 // How long a host-side wait for device work may last before it gives up
 // with an error (a healthy wait here is milliseconds; a device that stopped
 // answering must not hang the engine thread).

@@ -145,6 +145,10 @@ def _load() -> C.CDLL:
         "qvp_copy_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp]),
         "qvp_gather_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
         "qvp_scatter_blocks": (C.c_int, [vp, sz, u32, sz, vp, u32, vp, vp, vp]),
+        "qvp_swap_slot_bytes": (sz, [sz]),
+        "qvp_fetch_host": (C.c_int, [vp, vp, sz, vp]),
+        "qvp_compress_blocks": (C.c_int, [vp, sz, u32, sz, vp, vp, u32, vp, sz, vp, sz, u32, vp, vp, vp]),
+        "qvp_decompress_blocks": (C.c_int, [vp, sz, u32, sz, vp, vp, u32, vp, sz, vp, sz, u32, vp, vp, vp]),
         "qvp_kv_append": (C.c_int, [vp, sz, u32, P(BlockShape), u32, u32, u32, vp, vp, vp, vp, vp, vp]),
         "qvp_shard_gather_bytes": (C.c_int, [P(ShardDecodeArgs), P(sz)]),
         "qvp_shard_decode": (C.c_int, [P(ShardDecodeArgs), vp]),
@@ -174,6 +178,7 @@ EXPORTED = [
     "qvp_pool_create", "qvp_pool_destroy", "qvp_pool_base", "qvp_pool_stride", "qvp_pool_num_blocks",
     "qvp_pool_device", "qvp_pool_write", "qvp_pool_read", "qvp_decode_workspace_size",
     "qvp_decode_plan", "qvp_decode", "qvp_decode_noalloc", "qvp_prefill", "qvp_copy_blocks", "qvp_gather_blocks", "qvp_scatter_blocks",
+    "qvp_swap_slot_bytes", "qvp_compress_blocks", "qvp_decompress_blocks", "qvp_fetch_host",
     "qvp_kv_append", "qvp_shard_gather_bytes", "qvp_shard_decode", "qvp_shard_reassemble",
     "qvp_nccl_unique_id", "qvp_nccl_comm_init", "qvp_nccl_comm_destroy",
     "qvp_peer_group_create", "qvp_peer_group_open", "qvp_peer_group_destroy", "qvp_peer_group_output",

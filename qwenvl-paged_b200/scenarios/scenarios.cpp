@@ -193,7 +193,8 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_cow(int promp
 
 extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uint32_t pool_blocks, double occupancy,
                                                                          double preempt_fraction, int decode_batch,
-                                                                         int seed, char* out, size_t cap) {
+                                                                         int seed, int compressed, char* out,
+                                                                         size_t cap) {
     const BlockShape sh = bf16_shape(8);
     AllocatorConfig cfg;
     cfg.block_shape = sh;
@@ -202,6 +203,18 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
     MemoryAllocator alloc(cfg);
     if (!alloc.has_storage()) return emit("{\"error\": \"pool allocation failed: " + alloc.last_error() + "\"}", out, cap);
     const double pool_s = now_s() - t0;
+    {
+        // K/V-like contents (N(0,1) bf16) in every frame, so the compressed
+        // slots code what serving would swap: one 4 MiB tile, repeated
+        const std::size_t tile = std::size_t(4) << 20;
+        void* t = device_query(tile / 2, seed + 11);
+        const std::size_t total = static_cast<std::size_t>(pool_blocks) * alloc.block_stride();
+        for (std::size_t off = 0; off < total; off += tile)
+            cudaMemcpyAsync(alloc.pool_base() + off, t, std::min(tile, total - off), cudaMemcpyDeviceToDevice,
+                            alloc.stream());
+        cudaStreamSynchronize(alloc.stream());
+        cudaFree(t);
+    }
     KVCacheManager cache(alloc);
     std::mt19937 rng(seed);
     std::uniform_int_distribution<int> ctxd(512, 8192);
@@ -228,7 +241,7 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
     for (std::size_t i : pre) pre_blocks += (ctx[i] + 15) / 16;
 
     const double t1 = now_s();
-    DeviceSwapBackend swap(alloc, pre_blocks + 16);
+    DeviceSwapBackend swap(alloc, pre_blocks + 16, compressed ? SwapCoding::compressed : SwapCoding::raw);
     const double pin_s = now_s() - t1;
     if (!swap.ready()) return emit("{\"error\": \"pinned slab allocation failed\"}", out, cap);
     alloc.set_swap_backend(&swap);
@@ -358,10 +371,15 @@ extern "C" __attribute__((visibility("default"))) int qvp_scenario_swap(std::uin
         cudaEventDestroy(moved_ev);
     }
     const int derr = batch.device_error();
+    const auto link = swap.link_bytes();  // every pass above, both directions
     cudaFree(q);
     cudaFree(o);
     std::ostringstream js;
-    js << "{\"workload\": \"cfg5-swap-churn\", \"pool_blocks\": " << pool_blocks << ", \"block_bytes\": 65536"
+    js << "{\"workload\": \"cfg5-swap-churn\", \"coding\": \"" << (compressed ? "compressed" : "raw")
+       << "\", \"link_bytes_out\": " << link.first << ", \"link_bytes_in\": " << link.second
+       << ", \"block_bytes_out\": " << swap.bytes_out() << ", \"link_fraction\": "
+       << (swap.bytes_out() ? static_cast<double>(link.first) / swap.bytes_out() : 0.0)
+       << ", \"pool_blocks\": " << pool_blocks << ", \"block_bytes\": 65536"
        << ", \"pool_gib\": " << pool_blocks * 65536.0 / (1 << 30) << ", \"sequences\": " << seqs.size()
        << ", \"occupied_blocks\": " << pool_blocks - alloc.stats().free_blocks << ", \"preempted_sequences\": "
        << pre.size() << ", \"swapped_blocks\": " << swapped << ", \"swap_bytes_each_way\": " << moved

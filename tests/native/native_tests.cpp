@@ -173,10 +173,10 @@ NATIVE_TEST(copy_block_copies_bytes_and_batches_copies_into_one_launch) {
     CHECK(holds_bytes(m, 2, 99));
 }
 
-void swap_round_trip(bool device_backend) {
+void swap_round_trip(bool device_backend, SwapCoding coding = SwapCoding::raw) {
     MemoryAllocator m(config_of(shape_of(16, 1, 8, 128, 2), 6));
     HostSwapBackend host(4);
-    DeviceSwapBackend dev(m, 4);
+    DeviceSwapBackend dev(m, 4, coding);
     SwapBackend* backend = device_backend ? static_cast<SwapBackend*>(&dev) : &host;
     m.set_swap_backend(backend);
     const auto id = m.allocate();
@@ -201,6 +201,9 @@ void swap_round_trip(bool device_backend) {
 
 NATIVE_TEST(swap_out_then_in_restores_contents_host_backend) { swap_round_trip(false); }
 NATIVE_TEST(swap_out_then_in_restores_contents_device_backend) { swap_round_trip(true); }
+NATIVE_TEST(swap_out_then_in_restores_contents_compressed_device_backend) {
+    swap_round_trip(true, SwapCoding::compressed);
+}
 
 NATIVE_TEST(device_backend_capacity_and_slot_ids_follow_the_reference) {
     MemoryAllocator m(config_of(shape_of(4, 1, 1, 4), 8));
@@ -262,6 +265,61 @@ NATIVE_TEST(sequence_swap_out_and_in_restores_every_block_through_the_device_bac
     CHECK(dev.bytes_out() == 20u * 65536u && dev.bytes_in() == 20u * 65536u);
     cache.release_sequence(1);
     CHECK(m.stats().free_blocks == 64u && dev.resident_slots() == 0u);
+}
+
+// bf16 bit patterns of N(0,1) values (Box-Muller over a fixed LCG)
+std::vector<std::uint16_t> normal_bf16(std::size_t n, std::uint32_t seed) {
+    std::vector<std::uint16_t> v(n);
+    std::uint64_t x = 0x9E3779B97F4A7C15ull ^ seed;
+    auto uniform = [&] {
+        x = x * 6364136223846793005ull + 1442695040888963407ull;
+        return (static_cast<double>(x >> 11) + 0.5) / 9007199254740992.0;
+    };
+    for (std::size_t i = 0; i < n; ++i) {
+        const float f = static_cast<float>(std::sqrt(-2.0 * std::log(uniform())) * std::cos(6.283185307179586 * uniform()));
+        std::uint32_t bits;
+        std::memcpy(&bits, &f, 4);
+        v[i] = static_cast<std::uint16_t>(bits >> 16);
+    }
+    return v;
+}
+
+NATIVE_TEST(compressed_device_backend_restores_kv_bytes_and_sends_fewer_over_the_link) {
+    MemoryAllocator m(config_of(shape_of(16, 1, 8, 128, 2), 64));
+    DeviceSwapBackend dev(m, 64, SwapCoding::compressed);
+    m.set_swap_backend(&dev);
+    CHECK(dev.ready() && dev.coding() == SwapCoding::compressed);
+    KVCacheManager cache(m);
+    CHECK(cache.create_sequence(SequenceMetadata{1, 1, {}, {}}));
+    CHECK(cache.reserve_tokens(1, 16 * 20));
+    const std::size_t nb = m.block(0)->size_bytes();
+    std::map<std::uint32_t, std::vector<std::uint16_t>> want;
+    for (const auto& e : cache.cache_view(1)->block_table->entries()) {
+        auto v = normal_bf16(nb / 2, e.logical.index + 1);
+        if (e.logical.index == 3) std::fill(v.begin(), v.end(), 0);  // a zero block
+        if (e.logical.index == 4)                                   // random bytes: stored raw
+            for (std::size_t i = 0; i < v.size(); ++i) v[i] = static_cast<std::uint16_t>(i * 2654435761u >> 7);
+        CHECK(m.write_bytes(e.physical_id, 0, v.data(), nb));
+        want[e.logical.index] = std::move(v);
+    }
+    CHECK(cache.swap_out_sequence(1) == 20u);
+    CHECK(cache.create_sequence(SequenceMetadata{2, 2, {}, {}}));
+    CHECK(cache.reserve_tokens(2, 16 * 64));
+    for (const auto& e : cache.cache_view(2)->block_table->entries()) fill_bytes(m, e.physical_id, 200);
+    cache.release_sequence(2);
+    CHECK(cache.swap_in_sequence(1));
+    for (const auto& e : cache.cache_view(1)->block_table->entries()) {
+        std::vector<std::uint16_t> got(nb / 2);
+        CHECK(m.read_bytes(e.physical_id, 0, got.data(), nb));
+        CHECK(got == want[e.logical.index]);
+    }
+    CHECK(dev.bytes_out() == 20u * nb && dev.bytes_in() == 20u * nb);
+    const auto link = dev.link_bytes();
+    CHECK(link.first == link.second);
+    CHECK(link.first < 20u * nb * 8 / 10);  // 18 coded blocks near 0.75, one raw
+    CHECK(link.first > 20u * nb * 6 / 10);
+    CHECK(dev.last_error().empty());
+    cache.release_sequence(1);
 }
 
 NATIVE_TEST(cache_view_block_bytes_are_device_addresses_and_null_when_swapped) {

@@ -117,3 +117,21 @@ def test_kv_append_writes_the_new_token_rows():
         expect[blk, base:base + row] = v[b * row:(b + 1) * row]
     assert np.array_equal(got, expect)
     assert err.item() == 0
+
+
+def test_fetch_host_copies_pinned_bytes_at_any_alignment():
+    import torch
+
+    import qvp
+    rng = np.random.default_rng(4)
+    src = torch.from_numpy(rng.integers(0, 256, size=(3 << 20) + 64, dtype=np.uint8)).pin_memory()
+    dst = torch.zeros_like(src, device=_dev())
+    for off_s, off_d, n in ((0, 0, 0), (0, 0, 1), (3, 5, 17), (16, 32, 4096), (1, 0, (1 << 20) + 3),
+                            (0, 16, 3 << 20)):
+        dst.zero_()
+        assert qvp.lib.qvp_fetch_host(dst.data_ptr() + off_d, src.data_ptr() + off_s, n, _stream()) == 0
+        torch.cuda.synchronize()
+        got = dst.cpu().numpy()
+        assert np.array_equal(got[off_d:off_d + n], src.numpy()[off_s:off_s + n])
+        assert not got[:off_d].any() and not got[off_d + n:].any()
+    assert qvp.lib.qvp_fetch_host(None, src.data_ptr(), 16, _stream()) != 0

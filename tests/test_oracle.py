@@ -89,3 +89,47 @@ def test_oracle_copy_blocks_matches_memcpy():
     expect[1] = expect[7]
     oracle.port_copy_blocks(pool, 256, 8, 256, np.array([2, 5, 7, 1, 9, 0], dtype=np.int32))
     assert np.array_equal(pool.reshape(8, 256), expect)
+
+
+def _swap_block_256():
+    """128 bf16 values with low byte i: high bytes 0x3F/0xBF/0x40 by i % 3 for
+    i < 112, then 0x50..0x5F once each (16 singles: 4 escapes)."""
+    hi = [[0x3F, 0xBF, 0x40][i % 3] for i in range(112)] + [0x50 + j for j in range(16)]
+    vals = np.array([(h << 8) | i for i, h in enumerate(hi)], dtype=np.uint16)
+    return vals.view(np.uint8).copy()
+
+
+def test_swap_slot_format_known_answer():
+    block = _swap_block_256()
+    slot, esc = oracle.port_compress_block(block)
+    assert len(slot) == oracle.swap_slot_bytes(256) == 272
+    head = slot[:16].view(np.uint32)
+    # counts 38 (0x3F), 37 (0x40), 37 (0xBF): ties go to the smaller byte
+    assert list(head) == [oracle.SLOT_CODED, 4, 32 + 192 + 16, 0]
+    assert list(slot[16:32]) == [0x3F, 0x40, 0xBF] + list(range(0x50, 0x5C)) + [0]
+    codes = [{0: 0, 1: 2, 2: 1}[i % 3] for i in range(112)] + list(range(3, 15)) + [15] * 4
+    packed = [codes[2 * k] | (codes[2 * k + 1] << 4) for k in range(64)]
+    assert list(slot[32:96]) == packed
+    assert list(slot[96:224]) == list(range(128))
+    assert esc == {(124 + j) << 8 | (0x5C + j) for j in range(4)}
+    assert np.array_equal(oracle.port_decompress_slot(slot, 256), block)
+
+
+def test_swap_slot_raw_fallback_and_round_trips():
+    rng = np.random.default_rng(2)
+    for nb in (16, 48, 64, 256, 4096, 32768):
+        for kind in ("random", "gauss", "const"):
+            if kind == "random":
+                b = rng.integers(0, 256, nb, dtype=np.uint8)
+            elif kind == "gauss":
+                f = rng.normal(size=nb // 2).astype(np.float32)
+                b = (f.view(np.uint32) >> 16).astype(np.uint16).view(np.uint8)  # truncated to bf16
+            else:
+                b = np.full(nb, 7, dtype=np.uint8)
+            slot, _ = oracle.port_compress_block(b)
+            head = slot[:16].view(np.uint32)
+            if nb <= 64 or kind == "random":
+                assert head[0] == oracle.SLOT_RAW and head[2] == 16 + nb
+            else:
+                assert head[0] == oracle.SLOT_CODED and head[2] < 16 + nb
+            assert np.array_equal(oracle.port_decompress_slot(slot, nb), b)
