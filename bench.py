@@ -800,7 +800,7 @@ def run_prefill(args):
         "dtype": "bf16",
         "data": "synthetic: seeded N(0,1) K/V/Q, seeded scattered block tables",
         "config": {"workload": w.name, "batch": B, "prompt_tokens": L, "heads": "28q/4kv", "head_dim": 128,
-                   "kernel": "paged_prefill_fast (TMA + mma.sync, causal per-row limits)",
+                   "kernel": "paged_prefill_tc (TMA + tcgen05.mma, S and O in TMEM, causal per-row limits)",
                    "l2": "flushed (256 MiB write) before each timed launch"},
         "roofline": {"bound": "tensor", "achieved": round(tflops, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(tflops / peak, 4),

@@ -1274,9 +1274,14 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 
 int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape& shape, uint32_t hh,
                     CUtensorMap* map) {
+    return encode_pool_map_box(pool, num_blocks, shape, hh, 32, shape.head_dim / 64, map);
+}
+
+int encode_pool_map_box(const void* pool, uint32_t num_blocks, const qvp_block_shape& shape, uint32_t hh,
+                        uint32_t rows, uint32_t halves, CUtensorMap* map) {
     struct Key {
         const void* pool;
-        uint32_t num_blocks, layers, heads, dim, hh, rows;
+        uint32_t num_blocks, layers, heads, dim, hh, rows, halves;
     };
     static thread_local Key last{};
     static thread_local CUtensorMap cached;
@@ -1289,7 +1294,8 @@ int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape
     key.heads = shape.num_kv_heads;
     key.dim = shape.head_dim;
     key.hh = hh;
-    key.rows = 32;
+    key.rows = rows;
+    key.halves = halves;
     if (std::memcmp(&key, &last, sizeof(Key)) == 0) {
         *map = cached;
         return QVP_OK;
@@ -1300,7 +1306,7 @@ int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape
     const uint32_t H = shape.num_kv_heads;
     cuuint64_t dims[4] = {64, static_cast<cuuint64_t>(num_blocks) * shape.num_layers * 2 * 16, H, D / 64};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(H) * D * 2, static_cast<cuuint64_t>(D) * 2, 128};
-    cuuint32_t box[4] = {64, 32, hh, D / 64};
+    cuuint32_t box[4] = {64, rows, hh, halves};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(pool), dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,

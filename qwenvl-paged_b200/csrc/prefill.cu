@@ -21,6 +21,7 @@
 #include "attention_tile.cuh"
 #include "qvp_device.cuh"
 #include "qvp_internal.h"
+#include "tcgen05.cuh"
 
 #include <cuda.h>
 
@@ -49,6 +50,8 @@ struct PrefillParams {
     uint32_t group;
     uint32_t tile_tokens;  // TQ
     uint32_t max_qlen;     // row pitch (tokens) of q and out
+    uint32_t batch;
+    uint32_t hkv;
     float scale_log2;
 };
 
@@ -294,6 +297,363 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// paged_prefill_tc: the same tiles on the fifth-generation tensor cores.
+//
+// CTA = (tile of TQ = 128/G query tokens, kv head, sequence); its 128 rows
+// (token, query head) are the M of two tcgen05 GEMMs per step of 128 keys
+// (8 blocks):
+//   S = Q K^T  (M 128, N 128 keys, K head_dim)  -> TMEM columns [128 i, +128)
+//   O += P V   (M 128, N head_dim, K 128 keys)  -> TMEM columns [256, 384)
+// Warps 0-3 own one row each per thread (TMEM lane = row): they stage Q,
+// read S from TMEM, apply the causal mask and the online softmax, write P as
+// bf16 to shared memory and rescale O in TMEM when a row's running maximum
+// grows by more than 2^8 (below that the stale maximum is kept: P <= 256 and
+// the final division by the matching sum is exact). Warp 4 streams K and V
+// with TMA (one 16-row, 64-column box per block, K or V, head_dim half), so
+// that a stage is [half][128 keys][64] for K and for V: K is the K-major B
+// operand of the first GEMM, V the MN-major B operand of the second. Warp 5
+// allocates TMEM and one of its threads issues every MMA. S is double
+// buffered, so the softmax of step j overlaps the first GEMM of step j+1.
+// Keys past a row's position are masked in S; V rows past the context in
+// the last block are zeroed in shared memory before the second GEMM reads
+// them (P is 0 there, but 0 * NaN would not be).
+
+constexpr int kTcThreads = 192;
+constexpr uint32_t kTcRows = 128;
+constexpr uint32_t kTcKeys = 128;                 // keys per step (8 blocks)
+constexpr uint32_t kTcHalf = kTcRows * 128;       // one 64-column half of a 128-row tile: 16 KiB
+constexpr uint32_t kTcTile = 2 * kTcHalf;         // 128 rows x 128 bf16: 32 KiB
+constexpr uint32_t kTcStage = 2 * kTcTile;        // K and V of 128 keys
+constexpr uint32_t kTcBox = 16 * 128;             // one block's K (or V) rows of one half: 2 KiB
+constexpr uint32_t kTcCols = 512;                 // TMEM columns allocated
+
+template <int STAGES>
+struct TcLayout {
+    static constexpr uint32_t kQ = 0;
+    static constexpr uint32_t kKV = kTcTile;
+    static constexpr uint32_t kP = kKV + STAGES * kTcStage;
+    static constexpr uint32_t kBars = kP + 2 * kTcTile;
+    // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], o_done[2], q_ready, mma_idle
+    static constexpr uint32_t kNumBars = 2 * STAGES + 10;
+    static constexpr uint32_t kTmemSlot = kBars + 8 * kNumBars;
+    static constexpr uint32_t kSmem = kTmemSlot + 16 + 1024;
+};
+
+// byte offset of 16-byte chunk c (0..15) of row r in a K-major 128-row tile
+// with 128-byte swizzle
+__device__ __forceinline__ uint32_t tc_chunk(uint32_t r, uint32_t c) {
+    return (c >> 3) * kTcHalf + r * 128u + (((c & 7u) ^ (r & 7u)) << 4);
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+
+// every lane of the warp agrees whether the wait completed
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
+}
+
+template <int STAGES>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    paged_prefill_tc(const __grid_constant__ CUtensorMap tmap, const PrefillParams p, uint32_t ntiles) {
+    using L = TcLayout<STAGES>;
+    constexpr uint32_t D = 128;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    const uint32_t sb = smem_u32(smem);
+    const uint32_t bar0 = sb + L::kBars;
+    auto kv_full = [&](uint32_t s) { return bar0 + 8u * s; };
+    auto kv_empty = [&](uint32_t s) { return bar0 + 8u * (STAGES + s); };
+    auto s_full = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + i); };
+    auto s_free = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + 2 + i); };
+    auto p_full = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + 4 + i); };
+    auto o_done = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + 6 + i); };
+    const uint32_t q_ready = bar0 + 8u * (2 * STAGES + 8);
+    const uint32_t mma_idle = bar0 + 8u * (2 * STAGES + 9);
+
+    // longest tiles first: the tile index is the slowest-varying one, reversed
+    const uint32_t hkv = p.hkv;
+    const uint32_t per_tile = hkv * p.batch;
+    const uint32_t tile = ntiles - 1u - blockIdx.x / per_tile;
+    const uint32_t rem = blockIdx.x % per_tile;
+    const int kvh = static_cast<int>(rem % hkv);
+    const int b = static_cast<int>(rem / hkv);
+    const int ctx = p.ctx[b];
+    const int ql = p.qlen[b];
+    if (ctx <= 0 || static_cast<uint32_t>(ctx) > p.pitch * 16u || ql <= 0 || ql > ctx ||
+        static_cast<uint32_t>(ql) > p.max_qlen) {
+        if (threadIdx.x == 0 && tile == 0 && kvh == 0) record_error(p.err, kErrBadContext);
+        return;
+    }
+    const int G = static_cast<int>(p.group);
+    const int t0 = static_cast<int>(tile * p.tile_tokens);
+    if (t0 >= ql) return;
+    const int t1 = min(t0 + static_cast<int>(p.tile_tokens), ql);
+    const int rows = (t1 - t0) * G;
+    const int first_pos = ctx - ql;
+    const int last_pos = first_pos + t1 - 1;
+    const uint32_t nblk = static_cast<uint32_t>(last_pos) / 16u + 1u;
+    const uint32_t nsteps = (nblk + 7u) / 8u;
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(kv_full(s), 1);
+            mbar_init(kv_empty(s), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(s_full(i), 1);
+            mbar_init(s_free(i), kTcRows);
+            mbar_init(p_full(i), kTcRows);
+            mbar_init(o_done(i), 1);
+        }
+        mbar_init(q_ready, kTcRows);
+        mbar_init(mma_idle, 1);
+        mbar_fence_init();
+    }
+    if (warp == 5) {
+        tc::alloc(smem_u32(tmem_slot), kTcCols);
+        tc::relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ---- producer: K and V of 8 blocks per stage ----
+        if (lane == 0) {
+            prefetch_tensormap(&tmap);
+            const uint64_t policy = l2_policy_evict_last();  // every tile of the sequence reads the prefix
+            const int32_t* row = p.tables + static_cast<size_t>(b) * p.pitch;
+            uint32_t issued = 0;
+            for (uint32_t j = 0; j < nsteps; ++j) {
+                const uint32_t s = j % STAGES;
+                if (j >= STAGES && !mbar_wait_bounded(kv_empty(s), ((j / STAGES) - 1u) & 1u)) {
+                    record_error(p.err, kErrWaitTimeout);
+                    break;
+                }
+                const uint32_t nb = min(8u, nblk - j * 8u);
+                mbar_arrive_expect_tx(kv_full(s), nb * 4u * kTcBox);
+                const uint32_t kdst = sb + L::kKV + s * kTcStage;
+                for (uint32_t jj = 0; jj < nb; ++jj) {
+                    int32_t id = row[j * 8u + jj];
+                    if (static_cast<uint32_t>(id) >= p.num_blocks) {
+                        record_error(p.err, kErrBadBlockId);
+                        id = 0;
+                    }
+                    const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
+                    for (int dh = 0; dh < 2; ++dh) {
+                        const uint32_t off = static_cast<uint32_t>(dh) * kTcHalf + jj * kTcBox;
+                        tma_load_4d(kdst + off, &tmap, kv_full(s), 0, r, kvh, dh, policy);
+                        tma_load_4d(kdst + kTcTile + off, &tmap, kv_full(s), 0, r + 16, kvh, dh, policy);
+                    }
+                }
+                ++issued;
+            }
+            // no copy may still be landing when the CTA exits
+            for (uint32_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+                if (!mbar_wait_bounded(kv_full(j % STAGES), (j / STAGES) & 1u)) record_error(p.err, kErrWaitTimeout);
+        }
+    } else if (warp == 5) {
+        // ---- MMA issue (one thread) ----
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = tc::idesc_bf16_f32(kTcRows, kTcKeys, false, false);
+            constexpr uint32_t idesc_o = tc::idesc_bf16_f32(kTcRows, D, false, true);
+            bool ok = mbar_wait_bounded(q_ready, 0);
+            tc::fence_after_sync();
+            auto issue_pv = [&](uint32_t jp) -> bool {
+                const uint32_t i = jp & 1u, s = jp % STAGES;
+                if (!mbar_wait_bounded(p_full(i), (jp >> 1) & 1u)) return false;
+                tc::fence_after_sync();
+                const uint32_t nb = min(8u, nblk - jp * 8u);
+                const uint32_t pa = sb + L::kP + i * kTcTile;
+                const uint32_t vb = sb + L::kKV + s * kTcStage + kTcTile;
+                for (uint32_t kk = 0; kk < nb; ++kk) {
+                    const uint64_t ad = tc::smem_desc_sw128(pa + (kk >> 2) * kTcHalf + (kk & 3u) * 32u, 16, 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(vb + kk * kTcBox, kTcHalf, 1024);
+                    tc::mma_ss(tmem + 256u, ad, bd, idesc_o, jp > 0 || kk > 0);
+                }
+                tc::commit(o_done(i));
+                tc::commit(kv_empty(s));
+                return true;
+            };
+            for (uint32_t j = 0; ok && j < nsteps; ++j) {
+                const uint32_t s = j % STAGES, i = j & 1u;
+                if (!mbar_wait_bounded(kv_full(s), (j / STAGES) & 1u) ||
+                    (j >= 2 && !mbar_wait_bounded(s_free(i), ((j - 2) >> 1) & 1u))) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t kb = sb + L::kKV + s * kTcStage;
+                for (uint32_t kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * kTcHalf + (kk & 3u) * 32u;
+                    tc::mma_ss(tmem + i * kTcKeys, tc::smem_desc_sw128(sb + L::kQ + off, 16, 1024),
+                               tc::smem_desc_sw128(kb + off, 16, 1024), idesc_s, kk > 0);
+                }
+                tc::commit(s_full(i));
+                if (j >= 1 && !issue_pv(j - 1)) ok = false;
+            }
+            if (ok && !issue_pv(nsteps - 1)) ok = false;
+            if (!ok) record_error(p.err, kErrWaitTimeout);
+            // every MMA issued has completed before TMEM is released
+            tc::commit(mma_idle);
+            if (!mbar_wait_bounded(mma_idle, 0)) record_error(p.err, kErrWaitTimeout);
+        }
+    } else {
+        // ---- softmax: thread = row r of the tile ----
+        const uint32_t r = static_cast<uint32_t>(threadIdx.x);
+        const int rr = min(static_cast<int>(r), rows - 1);
+        const int tok = t0 + rr / G;
+        const int head = kvh * G + rr % G;
+        const bool live_row = static_cast<int>(r) < rows;
+        {
+            const uint4* qrow = reinterpret_cast<const uint4*>(
+                p.q + ((static_cast<size_t>(b) * p.max_qlen + tok) * p.hq + head) * D);
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) {
+                const uint4 v = live_row ? __ldg(qrow + c) : make_uint4(0, 0, 0, 0);
+                st_shared_v4(sb + L::kQ + tc_chunk(r, c), v);
+            }
+            tc::fence_async_smem();
+            mbar_arrive(q_ready);
+        }
+        const int pos = first_pos + tok;  // position of this row's token
+        const uint32_t lane_base = tmem + ((static_cast<uint32_t>(warp) * 32u) << 16);
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        // the block holding the last context key, if the tile loads it and
+        // it is partly past the context: its V rows past ctx are zeroed
+        const uint32_t partial_blk = static_cast<uint32_t>(ctx - 1) / 16u;
+        const bool zero_tail = (ctx & 15) != 0 && partial_blk == nblk - 1u;
+        for (uint32_t j = 0; ok && j < nsteps; ++j) {
+            const uint32_t i = j & 1u;
+            if (!warp_wait(s_full(i), (j >> 1) & 1u)) {
+                ok = false;
+                break;
+            }
+            tc::fence_after_sync();
+            uint32_t sv[kTcKeys];
+#pragma unroll
+            for (uint32_t c = 0; c < kTcKeys / 16; ++c)
+                tc::ld16(lane_base + i * kTcKeys + c * 16u, *reinterpret_cast<uint32_t(*)[16]>(&sv[c * 16]));
+            tc::wait_ld();
+            tc::reg_fence(sv);
+            float x[kTcKeys];
+#pragma unroll
+            for (uint32_t c = 0; c < kTcKeys; ++c) x[c] = __uint_as_float(sv[c]);
+            tc::fence_before_sync();
+            mbar_arrive(s_free(i));
+            const int lim = pos - static_cast<int>(j * kTcKeys);  // columns <= lim are visible
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < static_cast<int>(kTcKeys); ++c) {
+                x[c] = (c <= lim) ? x[c] * p.scale_log2 : -INFINITY;
+                mx = fmaxf(mx, x[c]);
+            }
+            const bool grow = mx > m_used + 8.f;
+            float factor = 1.f;
+            if (grow) {
+                factor = exp2f(m_used - mx);  // 0 on the first step
+                l *= factor;
+                m_used = mx;
+            }
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                // O holds steps < j: rescale it once the previous P V landed
+                if (!warp_wait(o_done((j - 1) & 1u), ((j - 1) >> 1) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+#pragma unroll 1
+                for (uint32_t c = 0; c < D / 16; ++c) {
+                    uint32_t v[16];
+                    tc::ld16(lane_base + 256u + c * 16u, v);
+                    tc::wait_ld();
+                    tc::reg_fence(v);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * factor);
+                    tc::st16(lane_base + 256u + c * 16u, v);
+                }
+                tc::wait_st();
+            }
+            // P buffer i is free once the P V of step j-2 has run
+            if (j >= 2 && !warp_wait(o_done(i), ((j - 2) >> 1) & 1u)) {
+                ok = false;
+                break;
+            }
+            const uint32_t pbuf = sb + L::kP + i * kTcTile;
+            float sum = 0.f;
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) {
+                float e8[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    // the sum takes the bf16 values the MMA multiplies, so
+                    // a row dominated by one key gives back its V exactly
+                    e8[e] = __bfloat162float(__float2bfloat16_rn(exp2f(x[c * 8 + e] - m_used)));
+                    sum += e8[e];
+                }
+                st_shared_v4(pbuf + tc_chunk(r, c),
+                             make_uint4(pack_bf16x2(e8[0], e8[1]), pack_bf16x2(e8[2], e8[3]),
+                                        pack_bf16x2(e8[4], e8[5]), pack_bf16x2(e8[6], e8[7])));
+            }
+            l += sum;
+            if (zero_tail && j == nsteps - 1u) {
+                const uint32_t jj = partial_blk - j * 8u;
+                const uint32_t first = static_cast<uint32_t>(ctx & 15);
+                const uint32_t n16 = (16u - first) * 8u;  // 16-byte chunks per half
+                const uint32_t vbase = sb + L::kKV + (j % STAGES) * kTcStage + kTcTile + jj * kTcBox;
+                for (uint32_t u = r; u < 2u * n16; u += kTcRows) {
+                    const uint32_t dh = u / n16, w = u % n16;
+                    st_shared_v4(vbase + dh * kTcHalf + (first + w / 8u) * 128u + (w % 8u) * 16u,
+                                 make_uint4(0, 0, 0, 0));
+                }
+            }
+            tc::fence_async_smem();
+            tc::fence_before_sync();
+            mbar_arrive(p_full(i));
+        }
+        if (ok) {
+            const uint32_t jl = nsteps - 1u;
+            ok = warp_wait(o_done(jl & 1u), (jl >> 1) & 1u);
+        }
+        if (!ok) {
+            record_error(p.err, kErrWaitTimeout);
+        } else {
+            tc::fence_after_sync();
+            const float inv = 1.f / l;
+            uint4* orow = reinterpret_cast<uint4*>(p.out + ((static_cast<size_t>(b) * p.max_qlen + tok) * p.hq + head) * D);
+#pragma unroll 1
+            for (uint32_t c = 0; c < D / 16; ++c) {
+                uint32_t v[16];
+                tc::ld16(lane_base + 256u + c * 16u, v);
+                tc::wait_ld();
+                tc::reg_fence(v);
+                uint32_t w[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e)
+                    w[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
+                if (live_row) {
+                    orow[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
+                    orow[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (warp == 5) tc::dealloc(tmem, kTcCols);
+}
+
+// ---------------------------------------------------------------------------
 
 constexpr int kGenWarps = 4;
 constexpr int kGenDimPerLane = 8;  // head_dim <= 256
@@ -409,6 +769,25 @@ int launch_prefill_fast(const qvp_prefill_args& a, const PrefillParams& pp, cuda
     return check_cuda(cudaGetLastError(), "launch prefill");
 }
 
+template <int STAGES>
+int launch_prefill_tc(const qvp_prefill_args& a, const PrefillParams& pp, cudaStream_t st) {
+    using L = TcLayout<STAGES>;
+    static_assert(L::kSmem <= 232448u - 1024u, "tcgen05 prefill shared memory");
+    static std::atomic<std::uint64_t> attr_done{0};
+    auto kern = paged_prefill_tc<STAGES>;
+    int rc = set_smem_limit_once(attr_done, reinterpret_cast<const void*>(kern), static_cast<int>(L::kSmem),
+                                 "cudaFuncSetAttribute(tcgen05 prefill)");
+    if (rc != QVP_OK) return rc;
+    CUtensorMap map;
+    rc = encode_pool_map_box(a.pool, a.num_blocks, a.shape, 1, 16, 1, &map);
+    if (rc != QVP_OK) return rc;
+    const uint32_t ntiles = ceil_div(a.max_query_len, pp.tile_tokens);
+    const uint64_t ctas = static_cast<uint64_t>(ntiles) * pp.hkv * pp.batch;
+    if (ctas > 0x7fffffffull) return fail(QVP_ERR_UNSUPPORTED, "prefill grid of %llu CTAs", (unsigned long long)ctas);
+    kern<<<static_cast<unsigned>(ctas), kTcThreads, L::kSmem, st>>>(map, pp, ntiles);
+    return check_cuda(cudaGetLastError(), "launch tcgen05 prefill");
+}
+
 }  // namespace
 
 }  // namespace qvp
@@ -461,7 +840,13 @@ extern "C" int qvp_prefill(const qvp_prefill_args* args, qvp_stream_t stream) {
         pp.group = G;
         pp.tile_tokens = static_cast<uint32_t>(kPrefillRows) / G;
         pp.max_qlen = a.max_query_len;
+        pp.batch = a.batch;
+        pp.hkv = sh.num_kv_heads;
         pp.scale_log2 = a.scale * 1.4426950408889634f;  // log2(e)
+        // head_dim 128 with 16-byte aligned rows: the tcgen05 kernel
+        if (sh.head_dim == 128 && (reinterpret_cast<uintptr_t>(a.query) & 15u) == 0 &&
+            (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0)
+            return launch_prefill_tc<2>(a, pp, st);
         return sh.head_dim == 128 ? launch_prefill_fast<128, 4, 5>(a, pp, st) : launch_prefill_fast<64, 4, 10>(a, pp, st);
     }
     PrefillGenericParams gp;

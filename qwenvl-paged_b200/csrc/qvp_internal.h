@@ -85,5 +85,9 @@ namespace qvp {
 // 128-byte swizzle. Needs unpadded blocks (stride == byte size).
 int encode_pool_map(const void* pool, uint32_t num_blocks, const qvp_block_shape& shape, uint32_t hh,
                     CUtensorMap_st* map);
+// The same map with a box of `rows` rows (16 = one K or V slice of a block,
+// 32 = both) and `halves` 64-element halves of head_dim.
+int encode_pool_map_box(const void* pool, uint32_t num_blocks, const qvp_block_shape& shape, uint32_t hh,
+                        uint32_t rows, uint32_t halves, CUtensorMap_st* map);
 
 }  // namespace qvp

@@ -1,0 +1,114 @@
+// Blackwell (sm_100a) fifth-generation tensor-core helpers: shared-memory
+// matrix descriptors, the kind::f16 instruction descriptor, tcgen05.mma with
+// its commit, and tensor-memory (TMEM) allocation, loads and stores. Written
+// from the PTX ISA's description of tcgen05; inline PTX only.
+#pragma once
+
+#include <cstdint>
+
+namespace qvp {
+namespace tc {
+
+// Shared-memory matrix descriptor, 128-byte swizzle. The tile starts on a
+// 1024-byte boundary (base offset 0); addresses and offsets are in bytes.
+//   K-major operand (rows of 64 bf16 = 128 bytes): lbo unused (16), sbo =
+//   distance between consecutive 8-row groups.
+//   MN-major operand: lbo = distance between 64-element groups along M/N,
+//   sbo = distance between consecutive 8-row groups along K.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((addr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;  // descriptor version for tcgen05
+    d |= 2ull << 61;  // 128-byte swizzle
+    return d;
+}
+
+// Instruction descriptor of kind::f16 with bf16 A and B and an f32
+// accumulator; a_mn / b_mn select MN-major operands.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(uint32_t m, uint32_t n, bool a_mn, bool b_mn) {
+    return (1u << 4)                  // D format: f32
+           | (1u << 7)                // A format: bf16
+           | (1u << 10)               // B format: bf16
+           | ((a_mn ? 1u : 0u) << 15)  // A major
+           | ((b_mn ? 1u : 0u) << 16)  // B major
+           | ((n >> 3) << 17)          // N / 8
+           | ((m >> 4) << 24);         // M / 16
+}
+
+// D[tmem] (+)= A[smem] * B[smem], issued by one thread.
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
+// Arrives once on the mbarrier when every tcgen05.mma this thread issued
+// before it has completed.
+__device__ __forceinline__ void commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+
+// Whole-warp TMEM allocation of `cols` columns (a power of two >= 32); the
+// base address is written to shared memory at `dst`.
+__device__ __forceinline__ void alloc(uint32_t dst, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst), "r"(cols)
+                 : "memory");
+}
+__device__ __forceinline__ void relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Generic-proxy writes to shared memory made visible to the tensor cores.
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Warp-collective: lane i of the warp reads 16 consecutive 32-bit columns of
+// TMEM lane (taddr.lane + i), starting at taddr's column.
+__device__ __forceinline__ void ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+}
+
+// After wait_ld: ties the loaded registers to a point after the wait, so the
+// compiler cannot move their uses above it.
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; ++i) asm volatile("" : "+r"(v[i]));
+}
+
+__device__ __forceinline__ void st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+}  // namespace tc
+}  // namespace qvp
