@@ -299,50 +299,58 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 // ---------------------------------------------------------------------------
 // paged_prefill_tc: the same tiles on the fifth-generation tensor cores.
 //
-// CTA = (tile of TQ = 128/G query tokens, kv head, sequence); its 128 rows
-// (token, query head) are the M of two tcgen05 GEMMs per step of 128 keys
-// (8 blocks):
-//   S = Q K^T  (M 128, N 128 keys, K head_dim)  -> TMEM columns [128 i, +128)
-//   O += P V   (M 128, N head_dim, K 128 keys)  -> TMEM columns [256, 384)
-// Warps 0-3 own one row each per thread (TMEM lane = row): they stage Q,
-// read S from TMEM, apply the causal mask and the online softmax, write P as
-// bf16 to shared memory and rescale O in TMEM when a row's running maximum
-// grows by more than 2^8 (below that the stale maximum is kept: P <= 256 and
-// the final division by the matching sum is exact). Warp 4 streams K and V
-// with TMA (one 16-row, 64-column box per block, K or V, head_dim half), so
-// that a stage is [half][128 keys][64] for K and for V: K is the K-major B
-// operand of the first GEMM, V the MN-major B operand of the second. Warp 5
-// allocates TMEM and one of its threads issues every MMA. S is double
-// buffered, so the softmax of step j overlaps the first GEMM of step j+1.
-// Keys past a row's position are masked in S; V rows past the context in
-// the last block are zeroed in shared memory before the second GEMM reads
-// them (P is 0 there, but 0 * NaN would not be).
+// CTA = (pair of tiles A, B of TQ = 128/G query tokens each, kv head,
+// sequence). A tile's 128 rows (token, query head) are the M of two tcgen05
+// GEMMs per step of 64 keys (4 blocks):
+//   S = Q K^T  (M 128, N 64 keys, K head_dim)  -> TMEM, double buffered
+//   O += P V   (M 128, N head_dim, K 64 keys)  -> TMEM
+// TMEM columns: S of tile t, buffer i at 128 t + 64 i; O of tile t at
+// 256 + 128 t. Warps 0-3 are tile A's softmax, warps 4-7 tile B's: a thread
+// owns one row (TMEM lane = row). They stage Q, read S from TMEM, apply the
+// causal mask and the online softmax, write P as bf16 to shared memory and
+// rescale O in TMEM when a row's running maximum grows by more than 2^8
+// (below that the stale maximum is kept: P <= 256, and the final division
+// by the sum of the same bf16 weights is exact). While one tile's softmax
+// runs, the tensor cores work on the other tile. Warp 8 streams K and V
+// with TMA, one 16-row, 64-column box per block, K or V and head_dim half,
+// so that a stage is [half][64 keys][64] for K and for V: K is the K-major
+// B operand of the first GEMM, V the MN-major B operand of the second; both
+// tiles read each stage. Warp 9 allocates TMEM and one of its threads issues
+// every MMA. Keys past a row's position are masked in S; V rows past the
+// context in the last block are zeroed in shared memory before the second
+// GEMM reads them (P is 0 there, but 0 * NaN would not be).
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 352;
 constexpr uint32_t kTcRows = 128;
-constexpr uint32_t kTcKeys = 128;                 // keys per step (8 blocks)
-constexpr uint32_t kTcHalf = kTcRows * 128;       // one 64-column half of a 128-row tile: 16 KiB
-constexpr uint32_t kTcTile = 2 * kTcHalf;         // 128 rows x 128 bf16: 32 KiB
-constexpr uint32_t kTcStage = 2 * kTcTile;        // K and V of 128 keys
-constexpr uint32_t kTcBox = 16 * 128;             // one block's K (or V) rows of one half: 2 KiB
-constexpr uint32_t kTcCols = 512;                 // TMEM columns allocated
+constexpr uint32_t kTcKeys = 64;                   // keys per step (4 blocks)
+constexpr uint32_t kTcBlocks = kTcKeys / 16;
+constexpr uint32_t kTcQHalf = kTcRows * 128;       // one 64-column half of Q: 16 KiB
+constexpr uint32_t kTcQ = 2 * kTcQHalf;            // 128 rows x 128 bf16
+constexpr uint32_t kTcKVHalf = kTcKeys * 128;      // one half of a K or V tile: 8 KiB
+constexpr uint32_t kTcKV = 2 * kTcKVHalf;          // K (or V) of one step: 16 KiB
+constexpr uint32_t kTcP = kTcRows * 128;           // 128 rows x 64 bf16
+constexpr uint32_t kTcBox = 16 * 128;              // one block's rows of one half: 2 KiB
+constexpr uint32_t kTcCols = 512;                  // TMEM columns allocated
 
 template <int STAGES>
 struct TcLayout {
-    static constexpr uint32_t kQ = 0;
-    static constexpr uint32_t kKV = kTcTile;
-    static constexpr uint32_t kP = kKV + STAGES * kTcStage;
-    static constexpr uint32_t kBars = kP + 2 * kTcTile;
-    // kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full[2], o_done[2], q_ready, mma_idle
-    static constexpr uint32_t kNumBars = 2 * STAGES + 10;
+    static constexpr uint32_t kQ = 0;                              // Q of tile t at kQ + t * kTcQ
+    static constexpr uint32_t kK = 2 * kTcQ;                       // K of stage s at kK + s * kTcKV
+    static constexpr uint32_t kV = kK + STAGES * kTcKV;            // V of stage s at kV + s * kTcKV
+    static constexpr uint32_t kP = kV + STAGES * kTcKV;            // P of tile t, buffer i at kP + (2t + i) kTcP
+    static constexpr uint32_t kBars = kP + 4 * kTcP;
+    // k_full[S], k_empty[S], v_full[S], v_empty[S],
+    // per tile {s_full[2], s_free[2], p_full[2], o_done[2], q_ready}, mma_idle
+    static constexpr uint32_t kTileBars = 9;
+    static constexpr uint32_t kNumBars = 4 * STAGES + 2 * kTileBars + 1;
     static constexpr uint32_t kTmemSlot = kBars + 8 * kNumBars;
     static constexpr uint32_t kSmem = kTmemSlot + 16 + 1024;
 };
 
-// byte offset of 16-byte chunk c (0..15) of row r in a K-major 128-row tile
-// with 128-byte swizzle
-__device__ __forceinline__ uint32_t tc_chunk(uint32_t r, uint32_t c) {
-    return (c >> 3) * kTcHalf + r * 128u + (((c & 7u) ^ (r & 7u)) << 4);
+// byte offset of 16-byte chunk c of row r in a K-major 128-row tile with
+// 128-byte swizzle whose 64-column halves are `half` bytes apart
+__device__ __forceinline__ uint32_t tc_chunk(uint32_t r, uint32_t c, uint32_t half) {
+    return (c >> 3) * half + r * 128u + (((c & 7u) ^ (r & 7u)) << 4);
 }
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
@@ -350,14 +358,38 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                  : "memory");
 }
 
+// 2^x on the special-function unit (flushes subnormal results to 0; the
+// softmax weights it makes are rounded to bf16, whose smallest normal is
+// 2^-126 as well)
+__device__ __forceinline__ float ex2_ftz(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 // every lane of the warp agrees whether the wait completed
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
     return __all_sync(0xffffffffu, mbar_wait_bounded(bar, parity));
 }
 
+struct TcTile {
+    int t0, rows;         // first query token, valid rows (0: no tile)
+    uint32_t nblk, steps; // blocks the tile sees, steps of kTcKeys
+};
+
+__device__ __forceinline__ TcTile tc_tile(int t0, int ql, int tq, int G, int first_pos) {
+    TcTile t{t0, 0, 0, 0};
+    if (t0 >= ql) return t;
+    const int t1 = min(t0 + tq, ql);
+    t.rows = (t1 - t0) * G;
+    t.nblk = static_cast<uint32_t>(first_pos + t1 - 1) / 16u + 1u;
+    t.steps = (t.nblk + kTcBlocks - 1) / kTcBlocks;
+    return t;
+}
+
 template <int STAGES>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    paged_prefill_tc(const __grid_constant__ CUtensorMap tmap, const PrefillParams p, uint32_t ntiles) {
+    paged_prefill_tc(const __grid_constant__ CUtensorMap tmap, const PrefillParams p, uint32_t npairs) {
     using L = TcLayout<STAGES>;
     constexpr uint32_t D = 128;
     extern __shared__ uint8_t smem_raw[];
@@ -365,58 +397,64 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const uint32_t sb = smem_u32(smem);
     const uint32_t bar0 = sb + L::kBars;
-    auto kv_full = [&](uint32_t s) { return bar0 + 8u * s; };
-    auto kv_empty = [&](uint32_t s) { return bar0 + 8u * (STAGES + s); };
-    auto s_full = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + i); };
-    auto s_free = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + 2 + i); };
-    auto p_full = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + 4 + i); };
-    auto o_done = [&](uint32_t i) { return bar0 + 8u * (2 * STAGES + 6 + i); };
-    const uint32_t q_ready = bar0 + 8u * (2 * STAGES + 8);
-    const uint32_t mma_idle = bar0 + 8u * (2 * STAGES + 9);
+    auto k_full = [&](uint32_t s) { return bar0 + 8u * s; };
+    auto k_empty = [&](uint32_t s) { return bar0 + 8u * (STAGES + s); };
+    auto v_full = [&](uint32_t s) { return bar0 + 8u * (2 * STAGES + s); };
+    auto v_empty = [&](uint32_t s) { return bar0 + 8u * (3 * STAGES + s); };
+    auto tbar = [&](uint32_t t, uint32_t k) { return bar0 + 8u * (4 * STAGES + t * L::kTileBars + k); };
+    auto s_full = [&](uint32_t t, uint32_t i) { return tbar(t, i); };
+    auto s_free = [&](uint32_t t, uint32_t i) { return tbar(t, 2 + i); };
+    auto p_full = [&](uint32_t t, uint32_t i) { return tbar(t, 4 + i); };
+    auto o_done = [&](uint32_t t, uint32_t i) { return tbar(t, 6 + i); };
+    auto q_ready = [&](uint32_t t) { return tbar(t, 8); };
+    const uint32_t mma_idle = bar0 + 8u * (L::kNumBars - 1);
 
-    // longest tiles first: the tile index is the slowest-varying one, reversed
+    // longest pairs first: the pair index is the slowest-varying one, reversed
     const uint32_t hkv = p.hkv;
-    const uint32_t per_tile = hkv * p.batch;
-    const uint32_t tile = ntiles - 1u - blockIdx.x / per_tile;
-    const uint32_t rem = blockIdx.x % per_tile;
+    const uint32_t per_pair = hkv * p.batch;
+    const uint32_t pair = npairs - 1u - blockIdx.x / per_pair;
+    const uint32_t rem = blockIdx.x % per_pair;
     const int kvh = static_cast<int>(rem % hkv);
     const int b = static_cast<int>(rem / hkv);
     const int ctx = p.ctx[b];
     const int ql = p.qlen[b];
     if (ctx <= 0 || static_cast<uint32_t>(ctx) > p.pitch * 16u || ql <= 0 || ql > ctx ||
         static_cast<uint32_t>(ql) > p.max_qlen) {
-        if (threadIdx.x == 0 && tile == 0 && kvh == 0) record_error(p.err, kErrBadContext);
+        if (threadIdx.x == 0 && pair == 0 && kvh == 0) record_error(p.err, kErrBadContext);
         return;
     }
     const int G = static_cast<int>(p.group);
-    const int t0 = static_cast<int>(tile * p.tile_tokens);
-    if (t0 >= ql) return;
-    const int t1 = min(t0 + static_cast<int>(p.tile_tokens), ql);
-    const int rows = (t1 - t0) * G;
+    const int tq = static_cast<int>(p.tile_tokens);
     const int first_pos = ctx - ql;
-    const int last_pos = first_pos + t1 - 1;
-    const uint32_t nblk = static_cast<uint32_t>(last_pos) / 16u + 1u;
-    const uint32_t nsteps = (nblk + 7u) / 8u;
+    const TcTile tA = tc_tile(static_cast<int>(pair) * 2 * tq, ql, tq, G, first_pos);
+    if (tA.rows == 0) return;
+    const TcTile tB = tc_tile(tA.t0 + tq, ql, tq, G, first_pos);
+    const uint32_t nblk = max(tA.nblk, tB.nblk);
+    const uint32_t nsteps = max(tA.steps, tB.steps);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kTmemSlot);
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(kv_full(s), 1);
-            mbar_init(kv_empty(s), 1);
+            mbar_init(k_full(s), 1);
+            mbar_init(k_empty(s), 1);
+            mbar_init(v_full(s), 1);
+            mbar_init(v_empty(s), 1);
         }
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(s_full(i), 1);
-            mbar_init(s_free(i), kTcRows);
-            mbar_init(p_full(i), kTcRows);
-            mbar_init(o_done(i), 1);
+        for (uint32_t t = 0; t < 2; ++t) {
+            for (uint32_t i = 0; i < 2; ++i) {
+                mbar_init(s_full(t, i), 1);
+                mbar_init(s_free(t, i), kTcRows);
+                mbar_init(p_full(t, i), kTcRows);
+                mbar_init(o_done(t, i), 1);
+            }
+            mbar_init(q_ready(t), kTcRows);
         }
-        mbar_init(q_ready, kTcRows);
         mbar_init(mma_idle, 1);
         mbar_fence_init();
     }
-    if (warp == 5) {
+    if (warp == 9) {
         tc::alloc(smem_u32(tmem_slot), kTcCols);
         tc::relinquish();
     }
@@ -425,116 +463,163 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
-        // ---- producer: K and V of 8 blocks per stage ----
-        if (lane == 0) {
-            prefetch_tensormap(&tmap);
-            const uint64_t policy = l2_policy_evict_last();  // every tile of the sequence reads the prefix
-            const int32_t* row = p.tables + static_cast<size_t>(b) * p.pitch;
-            uint32_t issued = 0;
-            for (uint32_t j = 0; j < nsteps; ++j) {
-                const uint32_t s = j % STAGES;
-                if (j >= STAGES && !mbar_wait_bounded(kv_empty(s), ((j / STAGES) - 1u) & 1u)) {
-                    record_error(p.err, kErrWaitTimeout);
-                    break;
-                }
-                const uint32_t nb = min(8u, nblk - j * 8u);
-                mbar_arrive_expect_tx(kv_full(s), nb * 4u * kTcBox);
-                const uint32_t kdst = sb + L::kKV + s * kTcStage;
-                for (uint32_t jj = 0; jj < nb; ++jj) {
-                    int32_t id = row[j * 8u + jj];
-                    if (static_cast<uint32_t>(id) >= p.num_blocks) {
-                        record_error(p.err, kErrBadBlockId);
-                        id = 0;
-                    }
-                    const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
-                    for (int dh = 0; dh < 2; ++dh) {
-                        const uint32_t off = static_cast<uint32_t>(dh) * kTcHalf + jj * kTcBox;
-                        tma_load_4d(kdst + off, &tmap, kv_full(s), 0, r, kvh, dh, policy);
-                        tma_load_4d(kdst + kTcTile + off, &tmap, kv_full(s), 0, r + 16, kvh, dh, policy);
-                    }
-                }
-                ++issued;
+    if (warp == 8 || warp == 10) {
+        // ---- producers (whole warps): warp 8 streams K, warp 10 V ----
+        // K and V have rings and warps of their own: a K slot is free once
+        // the step's first GEMMs have run, long before its V slot, and K
+        // loads never queue behind V loads. The block ids come 32 at a time,
+        // one per lane, a window ahead of their use, so no load of the table
+        // sits in front of a copy; lane jj issues the copies of block jj of
+        // the step.
+        const uint32_t kv = warp == 8 ? 0u : 1u;
+        if (lane == 0) prefetch_tensormap(&tmap);
+        const uint64_t policy = l2_policy_evict_last();  // every tile of the sequence reads the prefix
+        const int32_t* row = p.tables + static_cast<size_t>(b) * p.pitch;
+        auto window = [&](uint32_t w) -> int32_t {
+            const uint32_t k = w * 32u + static_cast<uint32_t>(lane);
+            return k < nblk ? __ldg(row + k) : 0;
+        };
+        int32_t win = window(0), win_next = window(1);
+        uint32_t cur = 0;
+        uint32_t issued = 0;
+        bool ok = true;
+        for (uint32_t j = 0; ok && j < nsteps; ++j) {
+            const uint32_t s = j % STAGES;
+            const uint32_t first = j * kTcBlocks;
+            if (first / 32u != cur) {
+                cur = first / 32u;
+                win = win_next;
+                win_next = window(cur + 1u);
             }
-            // no copy may still be landing when the CTA exits
-            for (uint32_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
-                if (!mbar_wait_bounded(kv_full(j % STAGES), (j / STAGES) & 1u)) record_error(p.err, kErrWaitTimeout);
-        }
-    } else if (warp == 5) {
-        // ---- MMA issue (one thread) ----
-        if (lane == 0) {
-            constexpr uint32_t idesc_s = tc::idesc_bf16_f32(kTcRows, kTcKeys, false, false);
-            constexpr uint32_t idesc_o = tc::idesc_bf16_f32(kTcRows, D, false, true);
-            bool ok = mbar_wait_bounded(q_ready, 0);
-            tc::fence_after_sync();
-            auto issue_pv = [&](uint32_t jp) -> bool {
-                const uint32_t i = jp & 1u, s = jp % STAGES;
-                if (!mbar_wait_bounded(p_full(i), (jp >> 1) & 1u)) return false;
-                tc::fence_after_sync();
-                const uint32_t nb = min(8u, nblk - jp * 8u);
-                const uint32_t pa = sb + L::kP + i * kTcTile;
-                const uint32_t vb = sb + L::kKV + s * kTcStage + kTcTile;
-                for (uint32_t kk = 0; kk < nb; ++kk) {
-                    const uint64_t ad = tc::smem_desc_sw128(pa + (kk >> 2) * kTcHalf + (kk & 3u) * 32u, 16, 1024);
-                    const uint64_t bd = tc::smem_desc_sw128(vb + kk * kTcBox, kTcHalf, 1024);
-                    tc::mma_ss(tmem + 256u, ad, bd, idesc_o, jp > 0 || kk > 0);
-                }
-                tc::commit(o_done(i));
-                tc::commit(kv_empty(s));
-                return true;
-            };
-            for (uint32_t j = 0; ok && j < nsteps; ++j) {
-                const uint32_t s = j % STAGES, i = j & 1u;
-                if (!mbar_wait_bounded(kv_full(s), (j / STAGES) & 1u) ||
-                    (j >= 2 && !mbar_wait_bounded(s_free(i), ((j - 2) >> 1) & 1u))) {
+            const uint32_t nb = min(kTcBlocks, nblk - first);
+            int32_t id = __shfl_sync(0xffffffffu, win, static_cast<int>((first + static_cast<uint32_t>(lane) % kTcBlocks) % 32u));
+            if (static_cast<uint32_t>(id) >= p.num_blocks) {
+                if (static_cast<uint32_t>(lane) < nb) record_error(p.err, kErrBadBlockId);
+                id = 0;
+            }
+            const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
+            {
+                const uint32_t full = kv == 0 ? k_full(s) : v_full(s);
+                if (j >= STAGES && !warp_wait(kv == 0 ? k_empty(s) : v_empty(s), ((j / STAGES) - 1u) & 1u)) {
                     ok = false;
                     break;
                 }
-                tc::fence_after_sync();
-                const uint32_t kb = sb + L::kKV + s * kTcStage;
-                for (uint32_t kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * kTcHalf + (kk & 3u) * 32u;
-                    tc::mma_ss(tmem + i * kTcKeys, tc::smem_desc_sw128(sb + L::kQ + off, 16, 1024),
-                               tc::smem_desc_sw128(kb + off, 16, 1024), idesc_s, kk > 0);
+                if (lane == 0) mbar_arrive_expect_tx(full, nb * 2u * kTcBox);
+                __syncwarp();
+                if (static_cast<uint32_t>(lane) < nb) {
+                    const uint32_t dst = sb + (kv == 0 ? L::kK : L::kV) + s * kTcKV + static_cast<uint32_t>(lane) * kTcBox;
+                    for (int dh = 0; dh < 2; ++dh)
+                        tma_load_4d(dst + static_cast<uint32_t>(dh) * kTcKVHalf, &tmap, full, 0,
+                                    r + 16 * static_cast<int>(kv), kvh, dh, policy);
                 }
-                tc::commit(s_full(i));
-                if (j >= 1 && !issue_pv(j - 1)) ok = false;
             }
-            if (ok && !issue_pv(nsteps - 1)) ok = false;
+            if (ok) ++issued;
+        }
+        if (!ok && lane == 0) record_error(p.err, kErrWaitTimeout);
+        // no copy may still be landing when the CTA exits
+        for (uint32_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+            if (!warp_wait(kv == 0 ? k_full(j % STAGES) : v_full(j % STAGES), (j / STAGES) & 1u) && lane == 0)
+                record_error(p.err, kErrWaitTimeout);
+    } else if (warp == 9) {
+        // ---- MMA issue (one thread) ----
+        // S of step j+2 is issued right after the P V of step j, two steps
+        // ahead of the softmax that reads it: an MMA group takes about a
+        // thousand cycles from issue to completion.
+        if (lane == 0) {
+            constexpr uint32_t idesc_s = tc::idesc_bf16_f32(kTcRows, kTcKeys, false, false);
+            constexpr uint32_t idesc_o = tc::idesc_bf16_f32(kTcRows, D, false, true);
+            const TcTile tiles[2] = {tA, tB};
+            const uint32_t ntiles = tB.rows > 0 ? 2u : 1u;
+            bool ok = mbar_wait_bounded(q_ready(0), 0) && (ntiles == 1 || mbar_wait_bounded(q_ready(1), 0));
+            tc::fence_after_sync();
+            auto gemm1 = [&](uint32_t j) -> bool {
+                const uint32_t s = j % STAGES, i = j & 1u;
+                if (!mbar_wait_bounded(k_full(s), (j / STAGES) & 1u)) return false;
+                const uint32_t kb = sb + L::kK + s * kTcKV;
+                for (uint32_t t = 0; t < ntiles; ++t) {
+                    if (j >= tiles[t].steps) continue;
+                    if (j >= 2 && !mbar_wait_bounded(s_free(t, i), ((j - 2) >> 1) & 1u)) return false;
+                    tc::fence_after_sync();
+                    const uint32_t qa = sb + L::kQ + t * kTcQ;
+                    for (uint32_t kk = 0; kk < D / 16; ++kk) {
+                        const uint64_t ad = tc::smem_desc_sw128(qa + (kk >> 2) * kTcQHalf + (kk & 3u) * 32u, 16, 1024);
+                        const uint64_t bd = tc::smem_desc_sw128(kb + (kk >> 2) * kTcKVHalf + (kk & 3u) * 32u, 16, 1024);
+                        tc::mma_ss(tmem + 128u * t + kTcKeys * i, ad, bd, idesc_s, kk > 0);
+                    }
+                    tc::commit(s_full(t, i));
+                }
+                tc::commit(k_empty(s));
+                return true;
+            };
+            for (uint32_t j = 0; ok && j < 2 && j < nsteps; ++j) ok = gemm1(j);
+            for (uint32_t j = 0; ok && j < nsteps; ++j) {
+                const uint32_t s = j % STAGES, i = j & 1u;
+                if (!mbar_wait_bounded(v_full(s), (j / STAGES) & 1u)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t vb = sb + L::kV + s * kTcKV;
+                for (uint32_t t = 0; ok && t < ntiles; ++t) {
+                    if (j >= tiles[t].steps) continue;
+                    if (!mbar_wait_bounded(p_full(t, i), (j >> 1) & 1u)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    const uint32_t nb = min(kTcBlocks, tiles[t].nblk - j * kTcBlocks);
+                    const uint32_t pa = sb + L::kP + (2 * t + i) * kTcP;
+                    for (uint32_t kk = 0; kk < nb; ++kk) {
+                        const uint64_t ad = tc::smem_desc_sw128(pa + kk * 32u, 16, 1024);
+                        const uint64_t bd = tc::smem_desc_sw128(vb + kk * kTcBox, kTcKVHalf, 1024);
+                        tc::mma_ss(tmem + 256u + 128u * t, ad, bd, idesc_o, j > 0 || kk > 0);
+                    }
+                    tc::commit(o_done(t, i));
+                }
+                if (!ok) break;
+                tc::commit(v_empty(s));
+                if (j + 2 < nsteps) ok = gemm1(j + 2);
+            }
             if (!ok) record_error(p.err, kErrWaitTimeout);
             // every MMA issued has completed before TMEM is released
             tc::commit(mma_idle);
             if (!mbar_wait_bounded(mma_idle, 0)) record_error(p.err, kErrWaitTimeout);
         }
     } else {
-        // ---- softmax: thread = row r of the tile ----
-        const uint32_t r = static_cast<uint32_t>(threadIdx.x);
-        const int rr = min(static_cast<int>(r), rows - 1);
-        const int tok = t0 + rr / G;
+        // ---- softmax: thread = row r of tile t ----
+        const uint32_t t = static_cast<uint32_t>(warp) >> 2;
+        const TcTile tile = t == 0 ? tA : tB;
+        const uint32_t r = static_cast<uint32_t>(threadIdx.x) & 127u;
+        const bool have = tile.rows > 0;
+        const int rr = have ? min(static_cast<int>(r), tile.rows - 1) : 0;
+        const int tok = tile.t0 + rr / G;
         const int head = kvh * G + rr % G;
-        const bool live_row = static_cast<int>(r) < rows;
-        {
+        const bool live_row = static_cast<int>(r) < tile.rows;
+        const uint32_t qs = sb + L::kQ + t * kTcQ;
+        if (have) {
             const uint4* qrow = reinterpret_cast<const uint4*>(
                 p.q + ((static_cast<size_t>(b) * p.max_qlen + tok) * p.hq + head) * D);
 #pragma unroll
             for (uint32_t c = 0; c < 16; ++c) {
                 const uint4 v = live_row ? __ldg(qrow + c) : make_uint4(0, 0, 0, 0);
-                st_shared_v4(sb + L::kQ + tc_chunk(r, c), v);
+                st_shared_v4(qs + tc_chunk(r, c, kTcQHalf), v);
             }
             tc::fence_async_smem();
-            mbar_arrive(q_ready);
+            mbar_arrive(q_ready(t));
         }
         const int pos = first_pos + tok;  // position of this row's token
-        const uint32_t lane_base = tmem + ((static_cast<uint32_t>(warp) * 32u) << 16);
+        const uint32_t lane_base = tmem + (((static_cast<uint32_t>(warp) & 3u) * 32u) << 16);
+        const uint32_t s_col = 128u * t, o_col = 256u + 128u * t;
+        const float sl2 = p.scale_log2;
+        const float grow_raw = 8.f / sl2;  // 2^8 in the exp2 domain, in raw score units
         float m_used = -INFINITY, l = 0.f;
         bool ok = true;
-        // the block holding the last context key, if the tile loads it and
+        // the block holding the last context key, if this tile reads it and
         // it is partly past the context: its V rows past ctx are zeroed
         const uint32_t partial_blk = static_cast<uint32_t>(ctx - 1) / 16u;
-        const bool zero_tail = (ctx & 15) != 0 && partial_blk == nblk - 1u;
-        for (uint32_t j = 0; ok && j < nsteps; ++j) {
+        const bool zero_tail = (ctx & 15) != 0 && partial_blk == tile.nblk - 1u;
+        for (uint32_t j = 0; have && ok && j < tile.steps; ++j) {
             const uint32_t i = j & 1u;
-            if (!warp_wait(s_full(i), (j >> 1) & 1u)) {
+            if (!warp_wait(s_full(t, i), (j >> 1) & 1u)) {
                 ok = false;
                 break;
             }
@@ -542,31 +627,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t sv[kTcKeys];
 #pragma unroll
             for (uint32_t c = 0; c < kTcKeys / 16; ++c)
-                tc::ld16(lane_base + i * kTcKeys + c * 16u, *reinterpret_cast<uint32_t(*)[16]>(&sv[c * 16]));
+                tc::ld16(lane_base + s_col + i * kTcKeys + c * 16u, *reinterpret_cast<uint32_t(*)[16]>(&sv[c * 16]));
             tc::wait_ld();
             tc::reg_fence(sv);
-            float x[kTcKeys];
-#pragma unroll
-            for (uint32_t c = 0; c < kTcKeys; ++c) x[c] = __uint_as_float(sv[c]);
             tc::fence_before_sync();
-            mbar_arrive(s_free(i));
+            mbar_arrive(s_free(t, i));
             const int lim = pos - static_cast<int>(j * kTcKeys);  // columns <= lim are visible
-            float mx = -INFINITY;
+            float x[kTcKeys];
+            if (lim >= static_cast<int>(kTcKeys) - 1) {
 #pragma unroll
-            for (int c = 0; c < static_cast<int>(kTcKeys); ++c) {
-                x[c] = (c <= lim) ? x[c] * p.scale_log2 : -INFINITY;
-                mx = fmaxf(mx, x[c]);
+                for (int c = 0; c < static_cast<int>(kTcKeys); ++c) x[c] = __uint_as_float(sv[c]);
+            } else {
+#pragma unroll
+                for (int c = 0; c < static_cast<int>(kTcKeys); ++c)
+                    x[c] = (c <= lim) ? __uint_as_float(sv[c]) : -INFINITY;
             }
-            const bool grow = mx > m_used + 8.f;
+            // eight independent chains, then a tree
+            float m8[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) m8[e] = x[e];
+#pragma unroll
+            for (int c = 8; c < static_cast<int>(kTcKeys); ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
+            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+            const bool grow = mx > m_used + grow_raw;
             float factor = 1.f;
             if (grow) {
-                factor = exp2f(m_used - mx);  // 0 on the first step
+                factor = exp2f((m_used - mx) * sl2);  // 0 on the first step
                 l *= factor;
                 m_used = mx;
             }
-            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+            const bool rescaled = j > 0 && __any_sync(0xffffffffu, grow);
+            if (rescaled) {
                 // O holds steps < j: rescale it once the previous P V landed
-                if (!warp_wait(o_done((j - 1) & 1u), ((j - 1) >> 1) & 1u)) {
+                if (!warp_wait(o_done(t, (j - 1) & 1u), ((j - 1) >> 1) & 1u)) {
                     ok = false;
                     break;
                 }
@@ -574,83 +668,87 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll 1
                 for (uint32_t c = 0; c < D / 16; ++c) {
                     uint32_t v[16];
-                    tc::ld16(lane_base + 256u + c * 16u, v);
+                    tc::ld16(lane_base + o_col + c * 16u, v);
                     tc::wait_ld();
                     tc::reg_fence(v);
 #pragma unroll
                     for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * factor);
-                    tc::st16(lane_base + 256u + c * 16u, v);
+                    tc::st16(lane_base + o_col + c * 16u, v);
                 }
                 tc::wait_st();
             }
-            // P buffer i is free once the P V of step j-2 has run
-            if (j >= 2 && !warp_wait(o_done(i), ((j - 2) >> 1) & 1u)) {
+            // P buffer i is free once the P V of step j-2 has run (a rescale
+            // above waited for step j-1, which completes after it)
+            if (j >= 2 && !rescaled && !warp_wait(o_done(t, i), ((j - 2) >> 1) & 1u)) {
                 ok = false;
                 break;
             }
-            const uint32_t pbuf = sb + L::kP + i * kTcTile;
-            float sum = 0.f;
+            const uint32_t pbuf = sb + L::kP + (2 * t + i) * kTcP;
+            const float msl = m_used * sl2;
+            float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) {
-                float e8[8];
+            for (uint32_t c = 0; c < kTcKeys / 8; ++c) {
+                uint32_t w[4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    // the sum takes the bf16 values the MMA multiplies, so
-                    // a row dominated by one key gives back its V exactly
-                    e8[e] = __bfloat162float(__float2bfloat16_rn(exp2f(x[c * 8 + e] - m_used)));
-                    sum += e8[e];
+                for (int e = 0; e < 4; ++e) {
+                    w[e] = pack_bf16x2(ex2_ftz(fmaf(x[c * 8 + 2 * e], sl2, -msl)),
+                                       ex2_ftz(fmaf(x[c * 8 + 2 * e + 1], sl2, -msl)));
+                    // the sum takes the bf16 values the MMA multiplies, so a
+                    // row dominated by one key gives back its V exactly
+                    sum[e] += __uint_as_float(w[e] << 16) + __uint_as_float(w[e] & 0xFFFF0000u);
                 }
-                st_shared_v4(pbuf + tc_chunk(r, c),
-                             make_uint4(pack_bf16x2(e8[0], e8[1]), pack_bf16x2(e8[2], e8[3]),
-                                        pack_bf16x2(e8[4], e8[5]), pack_bf16x2(e8[6], e8[7])));
+                st_shared_v4(pbuf + tc_chunk(r, c, 0), make_uint4(w[0], w[1], w[2], w[3]));
             }
-            l += sum;
-            if (zero_tail && j == nsteps - 1u) {
-                const uint32_t jj = partial_blk - j * 8u;
+            l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
+            if (zero_tail && j == tile.steps - 1u) {
+                const uint32_t jj = partial_blk - j * kTcBlocks;
                 const uint32_t first = static_cast<uint32_t>(ctx & 15);
                 const uint32_t n16 = (16u - first) * 8u;  // 16-byte chunks per half
-                const uint32_t vbase = sb + L::kKV + (j % STAGES) * kTcStage + kTcTile + jj * kTcBox;
+                const uint32_t vbase = sb + L::kV + (j % STAGES) * kTcKV + jj * kTcBox;
                 for (uint32_t u = r; u < 2u * n16; u += kTcRows) {
-                    const uint32_t dh = u / n16, w = u % n16;
-                    st_shared_v4(vbase + dh * kTcHalf + (first + w / 8u) * 128u + (w % 8u) * 16u,
+                    const uint32_t dh = u / n16, wq = u % n16;
+                    st_shared_v4(vbase + dh * kTcKVHalf + (first + wq / 8u) * 128u + (wq % 8u) * 16u,
                                  make_uint4(0, 0, 0, 0));
                 }
             }
             tc::fence_async_smem();
             tc::fence_before_sync();
-            mbar_arrive(p_full(i));
+            mbar_arrive(p_full(t, i));
         }
-        if (ok) {
-            const uint32_t jl = nsteps - 1u;
-            ok = warp_wait(o_done(jl & 1u), (jl >> 1) & 1u);
-        }
-        if (!ok) {
-            record_error(p.err, kErrWaitTimeout);
-        } else {
-            tc::fence_after_sync();
-            const float inv = 1.f / l;
-            uint4* orow = reinterpret_cast<uint4*>(p.out + ((static_cast<size_t>(b) * p.max_qlen + tok) * p.hq + head) * D);
+        if (have && ok) {
+            const uint32_t jl = tile.steps - 1u;
+            ok = warp_wait(o_done(t, jl & 1u), (jl >> 1) & 1u);
+            if (!ok) {
+                record_error(p.err, kErrWaitTimeout);
+            } else {
+                tc::fence_after_sync();
+                const float inv = 1.f / l;
+                uint4* orow = reinterpret_cast<uint4*>(
+                    p.out + ((static_cast<size_t>(b) * p.max_qlen + tok) * p.hq + head) * D);
 #pragma unroll 1
-            for (uint32_t c = 0; c < D / 16; ++c) {
-                uint32_t v[16];
-                tc::ld16(lane_base + 256u + c * 16u, v);
-                tc::wait_ld();
-                tc::reg_fence(v);
-                uint32_t w[8];
+                for (uint32_t c = 0; c < D / 16; ++c) {
+                    uint32_t v[16];
+                    tc::ld16(lane_base + o_col + c * 16u, v);
+                    tc::wait_ld();
+                    tc::reg_fence(v);
+                    uint32_t w[8];
 #pragma unroll
-                for (int e = 0; e < 8; ++e)
-                    w[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
-                if (live_row) {
-                    orow[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
-                    orow[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    for (int e = 0; e < 8; ++e)
+                        w[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
+                    if (live_row) {
+                        orow[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
+                        orow[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+                    }
                 }
             }
+        } else if (have) {
+            record_error(p.err, kErrWaitTimeout);
         }
     }
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    if (warp == 5) tc::dealloc(tmem, kTcCols);
+    if (warp == 9) tc::dealloc(tmem, kTcCols);
 }
 
 // ---------------------------------------------------------------------------
@@ -781,10 +879,10 @@ int launch_prefill_tc(const qvp_prefill_args& a, const PrefillParams& pp, cudaSt
     CUtensorMap map;
     rc = encode_pool_map_box(a.pool, a.num_blocks, a.shape, 1, 16, 1, &map);
     if (rc != QVP_OK) return rc;
-    const uint32_t ntiles = ceil_div(a.max_query_len, pp.tile_tokens);
-    const uint64_t ctas = static_cast<uint64_t>(ntiles) * pp.hkv * pp.batch;
+    const uint32_t npairs = ceil_div(ceil_div(a.max_query_len, pp.tile_tokens), 2);
+    const uint64_t ctas = static_cast<uint64_t>(npairs) * pp.hkv * pp.batch;
     if (ctas > 0x7fffffffull) return fail(QVP_ERR_UNSUPPORTED, "prefill grid of %llu CTAs", (unsigned long long)ctas);
-    kern<<<static_cast<unsigned>(ctas), kTcThreads, L::kSmem, st>>>(map, pp, ntiles);
+    kern<<<static_cast<unsigned>(ctas), kTcThreads, L::kSmem, st>>>(map, pp, npairs);
     return check_cuda(cudaGetLastError(), "launch tcgen05 prefill");
 }
 
@@ -846,7 +944,7 @@ extern "C" int qvp_prefill(const qvp_prefill_args* args, qvp_stream_t stream) {
         // head_dim 128 with 16-byte aligned rows: the tcgen05 kernel
         if (sh.head_dim == 128 && (reinterpret_cast<uintptr_t>(a.query) & 15u) == 0 &&
             (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0)
-            return launch_prefill_tc<2>(a, pp, st);
+            return launch_prefill_tc<3>(a, pp, st);
         return sh.head_dim == 128 ? launch_prefill_fast<128, 4, 5>(a, pp, st) : launch_prefill_fast<64, 4, 10>(a, pp, st);
     }
     PrefillGenericParams gp;
