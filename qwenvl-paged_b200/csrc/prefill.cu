@@ -301,34 +301,39 @@ __global__ void __launch_bounds__(kPrefillThreads, 1)
 //
 // CTA = (pair of tiles A, B of TQ = 128/G query tokens each, kv head,
 // sequence). A tile's 128 rows (token, query head) are the M of two tcgen05
-// GEMMs per step of 64 keys (4 blocks):
-//   S = Q K^T  (M 128, N 64 keys, K head_dim)  -> TMEM, double buffered
-//   O += P V   (M 128, N head_dim, K 64 keys)  -> TMEM
-// TMEM columns: S of tile t, buffer i at 128 t + 64 i; O of tile t at
-// 256 + 128 t. Warps 0-3 are tile A's softmax, warps 4-7 tile B's: a thread
-// owns one row (TMEM lane = row). They stage Q, read S from TMEM, apply the
-// causal mask and the online softmax, write P as bf16 to shared memory and
-// rescale O in TMEM when a row's running maximum grows by more than 2^8
-// (below that the stale maximum is kept: P <= 256, and the final division
-// by the sum of the same bf16 weights is exact). While one tile's softmax
-// runs, the tensor cores work on the other tile. Warp 8 streams K and V
-// with TMA, one 16-row, 64-column box per block, K or V and head_dim half,
-// so that a stage is [half][64 keys][64] for K and for V: K is the K-major
-// B operand of the first GEMM, V the MN-major B operand of the second; both
-// tiles read each stage. Warp 9 allocates TMEM and one of its threads issues
-// every MMA. Keys past a row's position are masked in S; V rows past the
-// context in the last block are zeroed in shared memory before the second
-// GEMM reads them (P is 0 there, but 0 * NaN would not be).
+// GEMMs per step of 128 keys (8 blocks):
+//   S = Q K^T  (M 128, N 128 keys, K head_dim; Q and K from shared memory)
+//   O += P V   (M 128, N head_dim, K 128 keys; P from TMEM, V from shared)
+// TMEM: S of tile t in columns [128 t, +128), overwritten by its P as bf16
+// pairs in the first 64 of them; O of tile t in [256 + 128 t, +128). Keeping
+// P in TMEM keeps it off shared memory, whose bandwidth the GEMM operands
+// need. The MMAs of one thread complete in issue order, and the issuer
+// runs P V(j) then S(j+1) of a tile back to back, so when a tile's S(j+1)
+// has landed its P V(j) has too: the softmax of a step waits for S alone.
+// While one tile's softmax runs, the tensor cores work on the other tile.
+//
+// Warps 0-3 are tile A's softmax, warps 4-7 tile B's: a thread owns one row
+// (TMEM lane = row). They stage Q, read S from TMEM, apply the causal mask
+// and the online softmax, write P and rescale O in TMEM when a row's running
+// maximum grows by more than 2^8 (below that the stale maximum is kept:
+// P <= 256, and the final division by the sum of the same bf16 weights is
+// exact). Warp 8 streams K and V with TMA (one 16-row, 64-column box per
+// block, K or V and head_dim half), each with a ring of its own, so that a
+// step's K is [half][128 keys][64]: the K-major B operand of the first GEMM;
+// V the same, the MN-major B operand of the second. Warp 9 allocates TMEM
+// and one of its threads issues every MMA. Keys past a row's position are
+// masked in S; V rows past the context in the last block are zeroed in
+// shared memory before the second GEMM reads them (P is 0 there, but 0 * NaN
+// would not be).
 
-constexpr int kTcThreads = 352;
+constexpr int kTcThreads = 320;
 constexpr uint32_t kTcRows = 128;
-constexpr uint32_t kTcKeys = 64;                   // keys per step (4 blocks)
+constexpr uint32_t kTcKeys = 128;                  // keys per step (8 blocks)
 constexpr uint32_t kTcBlocks = kTcKeys / 16;
 constexpr uint32_t kTcQHalf = kTcRows * 128;       // one 64-column half of Q: 16 KiB
 constexpr uint32_t kTcQ = 2 * kTcQHalf;            // 128 rows x 128 bf16
-constexpr uint32_t kTcKVHalf = kTcKeys * 128;      // one half of a K or V tile: 8 KiB
-constexpr uint32_t kTcKV = 2 * kTcKVHalf;          // K (or V) of one step: 16 KiB
-constexpr uint32_t kTcP = kTcRows * 128;           // 128 rows x 64 bf16
+constexpr uint32_t kTcKVHalf = kTcKeys * 128;      // one half of a K or V tile: 16 KiB
+constexpr uint32_t kTcKV = 2 * kTcKVHalf;          // K (or V) of one step: 32 KiB
 constexpr uint32_t kTcBox = 16 * 128;              // one block's rows of one half: 2 KiB
 constexpr uint32_t kTcCols = 512;                  // TMEM columns allocated
 
@@ -337,11 +342,9 @@ struct TcLayout {
     static constexpr uint32_t kQ = 0;                              // Q of tile t at kQ + t * kTcQ
     static constexpr uint32_t kK = 2 * kTcQ;                       // K of stage s at kK + s * kTcKV
     static constexpr uint32_t kV = kK + STAGES * kTcKV;            // V of stage s at kV + s * kTcKV
-    static constexpr uint32_t kP = kV + STAGES * kTcKV;            // P of tile t, buffer i at kP + (2t + i) kTcP
-    static constexpr uint32_t kBars = kP + 4 * kTcP;
-    // k_full[S], k_empty[S], v_full[S], v_empty[S],
-    // per tile {s_full[2], s_free[2], p_full[2], o_done[2], q_ready}, mma_idle
-    static constexpr uint32_t kTileBars = 9;
+    static constexpr uint32_t kBars = kV + STAGES * kTcKV;
+    // k_full[S], k_empty[S], v_full[S], v_empty[S], per tile {s_full, p_full, q_ready}, mma_idle
+    static constexpr uint32_t kTileBars = 3;
     static constexpr uint32_t kNumBars = 4 * STAGES + 2 * kTileBars + 1;
     static constexpr uint32_t kTmemSlot = kBars + 8 * kNumBars;
     static constexpr uint32_t kSmem = kTmemSlot + 16 + 1024;
@@ -373,8 +376,8 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity) {
 }
 
 struct TcTile {
-    int t0, rows;         // first query token, valid rows (0: no tile)
-    uint32_t nblk, steps; // blocks the tile sees, steps of kTcKeys
+    int t0, rows;          // first query token, valid rows (0: no tile)
+    uint32_t nblk, steps;  // blocks the tile sees, steps of kTcKeys
 };
 
 __device__ __forceinline__ TcTile tc_tile(int t0, int ql, int tq, int G, int first_pos) {
@@ -402,11 +405,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     auto v_full = [&](uint32_t s) { return bar0 + 8u * (2 * STAGES + s); };
     auto v_empty = [&](uint32_t s) { return bar0 + 8u * (3 * STAGES + s); };
     auto tbar = [&](uint32_t t, uint32_t k) { return bar0 + 8u * (4 * STAGES + t * L::kTileBars + k); };
-    auto s_full = [&](uint32_t t, uint32_t i) { return tbar(t, i); };
-    auto s_free = [&](uint32_t t, uint32_t i) { return tbar(t, 2 + i); };
-    auto p_full = [&](uint32_t t, uint32_t i) { return tbar(t, 4 + i); };
-    auto o_done = [&](uint32_t t, uint32_t i) { return tbar(t, 6 + i); };
-    auto q_ready = [&](uint32_t t) { return tbar(t, 8); };
+    auto s_full = [&](uint32_t t) { return tbar(t, 0); };
+    auto p_full = [&](uint32_t t) { return tbar(t, 1); };
+    auto q_ready = [&](uint32_t t) { return tbar(t, 2); };
     const uint32_t mma_idle = bar0 + 8u * (L::kNumBars - 1);
 
     // longest pairs first: the pair index is the slowest-varying one, reversed
@@ -443,12 +444,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(v_empty(s), 1);
         }
         for (uint32_t t = 0; t < 2; ++t) {
-            for (uint32_t i = 0; i < 2; ++i) {
-                mbar_init(s_full(t, i), 1);
-                mbar_init(s_free(t, i), kTcRows);
-                mbar_init(p_full(t, i), kTcRows);
-                mbar_init(o_done(t, i), 1);
-            }
+            mbar_init(s_full(t), 1);
+            mbar_init(p_full(t), kTcRows);
             mbar_init(q_ready(t), kTcRows);
         }
         mbar_init(mma_idle, 1);
@@ -463,15 +460,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 8 || warp == 10) {
-        // ---- producers (whole warps): warp 8 streams K, warp 10 V ----
-        // K and V have rings and warps of their own: a K slot is free once
-        // the step's first GEMMs have run, long before its V slot, and K
-        // loads never queue behind V loads. The block ids come 32 at a time,
-        // one per lane, a window ahead of their use, so no load of the table
-        // sits in front of a copy; lane jj issues the copies of block jj of
-        // the step.
-        const uint32_t kv = warp == 8 ? 0u : 1u;
+    if (warp == 8) {
+        // ---- producer (whole warp): K and V of kTcBlocks blocks per step ----
+        // K and V have rings of their own (a K slot is free once the step's
+        // first GEMMs have run, long before its V slot). The block ids come
+        // 32 at a time, one per lane, a window ahead of their use, so no load
+        // of the table sits in front of a copy; lane jj issues the copies of
+        // block jj of the step.
         if (lane == 0) prefetch_tensormap(&tmap);
         const uint64_t policy = l2_policy_evict_last();  // every tile of the sequence reads the prefix
         const int32_t* row = p.tables + static_cast<size_t>(b) * p.pitch;
@@ -481,7 +476,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         };
         int32_t win = window(0), win_next = window(1);
         uint32_t cur = 0;
-        uint32_t issued = 0;
+        uint32_t issued_k = 0, issued_v = 0;
         bool ok = true;
         for (uint32_t j = 0; ok && j < nsteps; ++j) {
             const uint32_t s = j % STAGES;
@@ -498,7 +493,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 id = 0;
             }
             const int r = (id * static_cast<int>(p.num_layers) + static_cast<int>(p.layer)) * 32;
-            {
+            for (uint32_t kv = 0; kv < 2; ++kv) {
                 const uint32_t full = kv == 0 ? k_full(s) : v_full(s);
                 if (j >= STAGES && !warp_wait(kv == 0 ? k_empty(s) : v_empty(s), ((j / STAGES) - 1u) & 1u)) {
                     ok = false;
@@ -512,19 +507,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         tma_load_4d(dst + static_cast<uint32_t>(dh) * kTcKVHalf, &tmap, full, 0,
                                     r + 16 * static_cast<int>(kv), kvh, dh, policy);
                 }
+                if (kv == 0)
+                    ++issued_k;
+                else
+                    ++issued_v;
             }
-            if (ok) ++issued;
         }
         if (!ok && lane == 0) record_error(p.err, kErrWaitTimeout);
         // no copy may still be landing when the CTA exits
-        for (uint32_t j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
-            if (!warp_wait(kv == 0 ? k_full(j % STAGES) : v_full(j % STAGES), (j / STAGES) & 1u) && lane == 0)
-                record_error(p.err, kErrWaitTimeout);
+        for (uint32_t j = issued_k > STAGES ? issued_k - STAGES : 0; j < issued_k; ++j)
+            if (!warp_wait(k_full(j % STAGES), (j / STAGES) & 1u) && lane == 0) record_error(p.err, kErrWaitTimeout);
+        for (uint32_t j = issued_v > STAGES ? issued_v - STAGES : 0; j < issued_v; ++j)
+            if (!warp_wait(v_full(j % STAGES), (j / STAGES) & 1u) && lane == 0) record_error(p.err, kErrWaitTimeout);
     } else if (warp == 9) {
-        // ---- MMA issue (one thread) ----
-        // S of step j+2 is issued right after the P V of step j, two steps
-        // ahead of the softmax that reads it: an MMA group takes about a
-        // thousand cycles from issue to completion.
+        // ---- MMA issue (one thread): per tile, P V(j) then S(j+1) ----
         if (lane == 0) {
             constexpr uint32_t idesc_s = tc::idesc_bf16_f32(kTcRows, kTcKeys, false, false);
             constexpr uint32_t idesc_o = tc::idesc_bf16_f32(kTcRows, D, false, true);
@@ -532,28 +528,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t ntiles = tB.rows > 0 ? 2u : 1u;
             bool ok = mbar_wait_bounded(q_ready(0), 0) && (ntiles == 1 || mbar_wait_bounded(q_ready(1), 0));
             tc::fence_after_sync();
-            auto gemm1 = [&](uint32_t j) -> bool {
-                const uint32_t s = j % STAGES, i = j & 1u;
+            // S(j) of tile t; the last tile that reads K(j) releases the slot
+            auto gemm1 = [&](uint32_t t, uint32_t j) -> bool {
+                const uint32_t s = j % STAGES;
                 if (!mbar_wait_bounded(k_full(s), (j / STAGES) & 1u)) return false;
+                tc::fence_after_sync();
                 const uint32_t kb = sb + L::kK + s * kTcKV;
-                for (uint32_t t = 0; t < ntiles; ++t) {
-                    if (j >= tiles[t].steps) continue;
-                    if (j >= 2 && !mbar_wait_bounded(s_free(t, i), ((j - 2) >> 1) & 1u)) return false;
-                    tc::fence_after_sync();
-                    const uint32_t qa = sb + L::kQ + t * kTcQ;
-                    for (uint32_t kk = 0; kk < D / 16; ++kk) {
-                        const uint64_t ad = tc::smem_desc_sw128(qa + (kk >> 2) * kTcQHalf + (kk & 3u) * 32u, 16, 1024);
-                        const uint64_t bd = tc::smem_desc_sw128(kb + (kk >> 2) * kTcKVHalf + (kk & 3u) * 32u, 16, 1024);
-                        tc::mma_ss(tmem + 128u * t + kTcKeys * i, ad, bd, idesc_s, kk > 0);
-                    }
-                    tc::commit(s_full(t, i));
+                const uint32_t qa = sb + L::kQ + t * kTcQ;
+                for (uint32_t kk = 0; kk < D / 16; ++kk) {
+                    const uint64_t ad = tc::smem_desc_sw128(qa + (kk >> 2) * kTcQHalf + (kk & 3u) * 32u, 16, 1024);
+                    const uint64_t bd = tc::smem_desc_sw128(kb + (kk >> 2) * kTcKVHalf + (kk & 3u) * 32u, 16, 1024);
+                    tc::mma_ss(tmem + 128u * t, ad, bd, idesc_s, kk > 0);
                 }
-                tc::commit(k_empty(s));
+                tc::commit(s_full(t));
+                if (t + 1 == ntiles || j >= tiles[t + 1].steps) tc::commit(k_empty(s));
                 return true;
             };
-            for (uint32_t j = 0; ok && j < 2 && j < nsteps; ++j) ok = gemm1(j);
+            for (uint32_t t = 0; ok && t < ntiles; ++t) ok = gemm1(t, 0);
             for (uint32_t j = 0; ok && j < nsteps; ++j) {
-                const uint32_t s = j % STAGES, i = j & 1u;
+                const uint32_t s = j % STAGES;
                 if (!mbar_wait_bounded(v_full(s), (j / STAGES) & 1u)) {
                     ok = false;
                     break;
@@ -561,23 +554,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t vb = sb + L::kV + s * kTcKV;
                 for (uint32_t t = 0; ok && t < ntiles; ++t) {
                     if (j >= tiles[t].steps) continue;
-                    if (!mbar_wait_bounded(p_full(t, i), (j >> 1) & 1u)) {
+                    if (!mbar_wait_bounded(p_full(t), j & 1u)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
                     const uint32_t nb = min(kTcBlocks, tiles[t].nblk - j * kTcBlocks);
-                    const uint32_t pa = sb + L::kP + (2 * t + i) * kTcP;
                     for (uint32_t kk = 0; kk < nb; ++kk) {
-                        const uint64_t ad = tc::smem_desc_sw128(pa + kk * 32u, 16, 1024);
                         const uint64_t bd = tc::smem_desc_sw128(vb + kk * kTcBox, kTcKVHalf, 1024);
-                        tc::mma_ss(tmem + 256u + 128u * t, ad, bd, idesc_o, j > 0 || kk > 0);
+                        tc::mma_ts(tmem + 256u + 128u * t, tmem + 128u * t + kk * 8u, bd, idesc_o, j > 0 || kk > 0);
                     }
-                    tc::commit(o_done(t, i));
+                    // the last tile that reads V(j) releases the slot
+                    if (t + 1 == ntiles || j >= tiles[t + 1].steps) tc::commit(v_empty(s));
+                    if (j + 1 < tiles[t].steps) ok = gemm1(t, j + 1);
+                    else tc::commit(s_full(t));  // the tile's last P V has landed
                 }
-                if (!ok) break;
-                tc::commit(v_empty(s));
-                if (j + 2 < nsteps) ok = gemm1(j + 2);
             }
             if (!ok) record_error(p.err, kErrWaitTimeout);
             // every MMA issued has completed before TMEM is released
@@ -598,11 +589,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (have) {
             const uint4* qrow = reinterpret_cast<const uint4*>(
                 p.q + ((static_cast<size_t>(b) * p.max_qlen + tok) * p.hq + head) * D);
+            uint4 qv[16];
 #pragma unroll
-            for (uint32_t c = 0; c < 16; ++c) {
-                const uint4 v = live_row ? __ldg(qrow + c) : make_uint4(0, 0, 0, 0);
-                st_shared_v4(qs + tc_chunk(r, c, kTcQHalf), v);
-            }
+            for (uint32_t c = 0; c < 16; ++c) qv[c] = live_row ? __ldg(qrow + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (uint32_t c = 0; c < 16; ++c) st_shared_v4(qs + tc_chunk(r, c, kTcQHalf), qv[c]);
             tc::fence_async_smem();
             mbar_arrive(q_ready(t));
         }
@@ -618,8 +609,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t partial_blk = static_cast<uint32_t>(ctx - 1) / 16u;
         const bool zero_tail = (ctx & 15) != 0 && partial_blk == tile.nblk - 1u;
         for (uint32_t j = 0; have && ok && j < tile.steps; ++j) {
-            const uint32_t i = j & 1u;
-            if (!warp_wait(s_full(t, i), (j >> 1) & 1u)) {
+            // S(j) landed, and with it the P V of step j-1 (issued before it)
+            if (!warp_wait(s_full(t), j & 1u)) {
                 ok = false;
                 break;
             }
@@ -627,27 +618,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t sv[kTcKeys];
 #pragma unroll
             for (uint32_t c = 0; c < kTcKeys / 16; ++c)
-                tc::ld16(lane_base + s_col + i * kTcKeys + c * 16u, *reinterpret_cast<uint32_t(*)[16]>(&sv[c * 16]));
+                tc::ld16(lane_base + s_col + c * 16u, *reinterpret_cast<uint32_t(*)[16]>(&sv[c * 16]));
             tc::wait_ld();
             tc::reg_fence(sv);
-            tc::fence_before_sync();
-            mbar_arrive(s_free(t, i));
             const int lim = pos - static_cast<int>(j * kTcKeys);  // columns <= lim are visible
-            float x[kTcKeys];
-            if (lim >= static_cast<int>(kTcKeys) - 1) {
-#pragma unroll
-                for (int c = 0; c < static_cast<int>(kTcKeys); ++c) x[c] = __uint_as_float(sv[c]);
-            } else {
+            if (lim < static_cast<int>(kTcKeys) - 1) {
 #pragma unroll
                 for (int c = 0; c < static_cast<int>(kTcKeys); ++c)
-                    x[c] = (c <= lim) ? __uint_as_float(sv[c]) : -INFINITY;
+                    if (c > lim) sv[c] = __float_as_uint(-INFINITY);
             }
             // eight independent chains, then a tree
             float m8[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) m8[e] = x[e];
+            for (int e = 0; e < 8; ++e) m8[e] = __uint_as_float(sv[e]);
 #pragma unroll
-            for (int c = 8; c < static_cast<int>(kTcKeys); ++c) m8[c & 7] = fmaxf(m8[c & 7], x[c]);
+            for (int c = 8; c < static_cast<int>(kTcKeys); ++c) m8[c & 7] = fmaxf(m8[c & 7], __uint_as_float(sv[c]));
             const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                                    fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
             const bool grow = mx > m_used + grow_raw;
@@ -657,14 +642,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 l *= factor;
                 m_used = mx;
             }
-            const bool rescaled = j > 0 && __any_sync(0xffffffffu, grow);
-            if (rescaled) {
-                // O holds steps < j: rescale it once the previous P V landed
-                if (!warp_wait(o_done(t, (j - 1) & 1u), ((j - 1) >> 1) & 1u)) {
-                    ok = false;
-                    break;
-                }
-                tc::fence_after_sync();
+            if (j > 0 && __any_sync(0xffffffffu, grow)) {
+                // O holds steps < j (their P V landed before S(j)): rescale it
 #pragma unroll 1
                 for (uint32_t c = 0; c < D / 16; ++c) {
                     uint32_t v[16];
@@ -675,29 +654,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__uint_as_float(v[e]) * factor);
                     tc::st16(lane_base + o_col + c * 16u, v);
                 }
-                tc::wait_st();
             }
-            // P buffer i is free once the P V of step j-2 has run (a rescale
-            // above waited for step j-1, which completes after it)
-            if (j >= 2 && !rescaled && !warp_wait(o_done(t, i), ((j - 2) >> 1) & 1u)) {
-                ok = false;
-                break;
-            }
-            const uint32_t pbuf = sb + L::kP + (2 * t + i) * kTcP;
             const float msl = m_used * sl2;
             float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (uint32_t c = 0; c < kTcKeys / 8; ++c) {
-                uint32_t w[4];
+            for (uint32_t c = 0; c < kTcKeys / 32; ++c) {
+                uint32_t w[16];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    w[e] = pack_bf16x2(ex2_ftz(fmaf(x[c * 8 + 2 * e], sl2, -msl)),
-                                       ex2_ftz(fmaf(x[c * 8 + 2 * e + 1], sl2, -msl)));
+                for (int e = 0; e < 16; ++e) {
+                    w[e] = pack_bf16x2(ex2_ftz(fmaf(__uint_as_float(sv[c * 32 + 2 * e]), sl2, -msl)),
+                                       ex2_ftz(fmaf(__uint_as_float(sv[c * 32 + 2 * e + 1]), sl2, -msl)));
                     // the sum takes the bf16 values the MMA multiplies, so a
                     // row dominated by one key gives back its V exactly
-                    sum[e] += __uint_as_float(w[e] << 16) + __uint_as_float(w[e] & 0xFFFF0000u);
+                    sum[e & 3] += __uint_as_float(w[e] << 16) + __uint_as_float(w[e] & 0xFFFF0000u);
                 }
-                st_shared_v4(pbuf + tc_chunk(r, c, 0), make_uint4(w[0], w[1], w[2], w[3]));
+                tc::st16(lane_base + s_col + c * 16u, w);  // P over the S just read
             }
             l += (sum[0] + sum[1]) + (sum[2] + sum[3]);
             if (zero_tail && j == tile.steps - 1u) {
@@ -710,14 +681,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     st_shared_v4(vbase + dh * kTcKVHalf + (first + wq / 8u) * 128u + (wq % 8u) * 16u,
                                  make_uint4(0, 0, 0, 0));
                 }
+                tc::fence_async_smem();
             }
-            tc::fence_async_smem();
+            tc::wait_st();
             tc::fence_before_sync();
-            mbar_arrive(p_full(t, i));
+            mbar_arrive(p_full(t));
         }
         if (have && ok) {
-            const uint32_t jl = tile.steps - 1u;
-            ok = warp_wait(o_done(t, jl & 1u), (jl >> 1) & 1u);
+            // the tile's last P V: the issuer commits s_full once more after it
+            ok = warp_wait(s_full(t), tile.steps & 1u);
             if (!ok) {
                 record_error(p.err, kErrWaitTimeout);
             } else {
@@ -725,19 +697,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const float inv = 1.f / l;
                 uint4* orow = reinterpret_cast<uint4*>(
                     p.out + ((static_cast<size_t>(b) * p.max_qlen + tok) * p.hq + head) * D);
-#pragma unroll 1
-                for (uint32_t c = 0; c < D / 16; ++c) {
-                    uint32_t v[16];
-                    tc::ld16(lane_base + o_col + c * 16u, v);
-                    tc::wait_ld();
-                    tc::reg_fence(v);
-                    uint32_t w[8];
+                uint32_t ov[D];
 #pragma unroll
-                    for (int e = 0; e < 8; ++e)
-                        w[e] = pack_bf16x2(__uint_as_float(v[2 * e]) * inv, __uint_as_float(v[2 * e + 1]) * inv);
-                    if (live_row) {
-                        orow[2 * c] = make_uint4(w[0], w[1], w[2], w[3]);
-                        orow[2 * c + 1] = make_uint4(w[4], w[5], w[6], w[7]);
+                for (uint32_t c = 0; c < D / 16; ++c)
+                    tc::ld16(lane_base + o_col + c * 16u, *reinterpret_cast<uint32_t(*)[16]>(&ov[c * 16]));
+                tc::wait_ld();
+                tc::reg_fence(ov);
+                if (live_row) {
+#pragma unroll
+                    for (uint32_t c = 0; c < D / 8; ++c) {
+                        uint32_t w[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            w[e] = pack_bf16x2(__uint_as_float(ov[8 * c + 2 * e]) * inv,
+                                               __uint_as_float(ov[8 * c + 2 * e + 1]) * inv);
+                        orow[c] = make_uint4(w[0], w[1], w[2], w[3]);
                     }
                 }
             }
@@ -944,7 +918,7 @@ extern "C" int qvp_prefill(const qvp_prefill_args* args, qvp_stream_t stream) {
         // head_dim 128 with 16-byte aligned rows: the tcgen05 kernel
         if (sh.head_dim == 128 && (reinterpret_cast<uintptr_t>(a.query) & 15u) == 0 &&
             (reinterpret_cast<uintptr_t>(a.out) & 15u) == 0)
-            return launch_prefill_tc<3>(a, pp, st);
+            return launch_prefill_tc<2>(a, pp, st);
         return sh.head_dim == 128 ? launch_prefill_fast<128, 4, 5>(a, pp, st) : launch_prefill_fast<64, 4, 10>(a, pp, st);
     }
     PrefillGenericParams gp;

@@ -48,6 +48,18 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]: A is M rows in TMEM lanes, two 16-bit
+// elements per 32-bit column (K = 16 takes 8 columns).
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                       bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate ? 1u : 0u)
+        : "memory");
+}
+
 // Arrives once on the mbarrier when every tcgen05.mma this thread issued
 // before it has completed.
 __device__ __forceinline__ void commit(uint32_t bar) {
